@@ -1,0 +1,355 @@
+#!/usr/bin/env python
+"""Benchmark: batched Householder QR (geqrf + Q formation) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+One step = one fused QR (``qr_b200.qr``: (H, tau) in torch.geqrf form plus the
+explicit Q, i.e. 8/3 n^3 flops per matrix) of one batch of the configuration.
+Default configuration: ``b4096_n64`` (4096 i.i.d. N(0,1) 64x64 fp32 matrices).
+
+Multi-GPU (torchrun, one process per GPU): weak scaling -- every rank factors its
+own full batch (seed + rank); there is no collective on the data path, only a
+barrier and a max-reduction of the timings.  ``value`` = all ranks' matrices /
+max-over-ranks time.
+
+Timing: per step, the L2 is flushed (256 MiB write, untimed, as the reference
+harness's clear_l2_cache does) and the step is bracketed by CUDA events on the
+launching stream; ms_per_step is the mean of the K step durations, max over ranks.
+
+``--impl reference``: the reference arm -- CPU ``torch.linalg.qr`` (the
+comparator the reference names) on the host cores, rank 0 only, one bounded
+sample of the workload per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG = ROOT / "linalg-gpu-comp_b200"
+for _p in (str(ROOT), str(PKG)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "BASELINE.json").exists() \
+    else "batched QR matrices/s"
+DEFAULT_CONFIG = "b4096_n64"
+
+
+def flops_per_matrix(n: int) -> float:
+    return 8.0 / 3.0 * n ** 3
+
+
+def bytes_per_matrix(n: int) -> int:
+    """Algorithmic HBM bytes of the fused QR: read A, write H, tau and Q."""
+    return 12 * n * n + 4 * n
+
+
+def kernel_launches(n: int) -> int:
+    """libqrb200 kernels one fused QR enqueues (see csrc/qrb_api.cu dispatch)."""
+    if n <= 64:
+        return 1
+    np_ = (n + 31) // 32
+    return np_ + (np_ - 1) + np_      # panels + trailing updates + orgqr blocks
+
+
+def dominant_kernel(n: int) -> str:
+    return "small_qr_kernel" if n <= 64 else "apply_kernel"
+
+
+def load_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def load_traffic(config: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        e = d.get(config)
+        if e:
+            return e.get("dram_bytes_per_launch")
+    return None
+
+
+# ---------------------------------------------------------------------------
+# clocks (read-only NVML sampling during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x0000000000000004: "sw_power_cap", 0x0000000000000008: "hw_slowdown",
+        0x0000000000000020: "sw_thermal_slowdown", 0x0000000000000040: "hw_thermal_slowdown",
+        0x0000000000000080: "hw_power_brake_slowdown", 0x0000000000000002: "applications_clocks_setting",
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.02):
+        self.samples, self.reasons, self.ok = [], set(), False
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._period = period_s
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self._nv = None
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(self._period)
+
+    def __enter__(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init(gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        return dist, rank, world, local
+    return None, 0, 1, 0
+
+
+def reduce_max(dist, x: float, device) -> float:
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist, device):
+    if dist is not None:
+        dist.barrier(device_ids=[device.index])
+    torch.cuda.synchronize(device)
+
+
+# ---------------------------------------------------------------------------
+# CPU legs
+# ---------------------------------------------------------------------------
+def cpu_sample(config: str, seed: int, target_s: float):
+    """Bounded sample of the workload on the host: (matrices, A_cpu)."""
+    from qr_b200.inputs import CONFIGS, config_input
+    batch, n, _ = CONFIGS[config]
+    from oracle import cpu_ref
+    probe = config_input(config, seed=seed, device="cpu", batch=min(batch, 8))
+    cpu_ref.cpu_qr(probe)
+    t0 = time.perf_counter()
+    cpu_ref.cpu_qr(probe)
+    per = max((time.perf_counter() - t0) / probe.shape[0], 1e-7)
+    m = int(max(1, min(batch, target_s / per)))
+    return m, config_input(config, seed=seed, device="cpu", batch=m)
+
+
+def cpu_baseline(config: str, seed: int, budget_s: float = 12.0) -> dict:
+    from oracle import cpu_ref
+    threads = cpu_ref.set_threads()
+    m, A = cpu_sample(config, seed, budget_s / 6)
+    sec = cpu_ref.time_cpu_qr(A, min_seconds=budget_s * 0.8, max_iters=10_000)
+    return {"value": m / sec, "unit": "matrices/s", "cores": threads, "kind": "reference",
+            "sample": f"torch.linalg.qr (LAPACK sgeqrf+sorgqr, fp32) on {m} of the {config} matrices, "
+                      f"repeated for ~{budget_s * 0.8:.0f} s on {threads} host threads"}
+
+
+def run_reference(args) -> dict | None:
+    dist, rank, world, local = dist_init(args.gpus)
+    if rank != 0:
+        return None
+    from oracle import cpu_ref
+    from qr_b200.inputs import CONFIGS
+    batch, n, _ = CONFIGS[args.config]
+    threads = cpu_ref.set_threads()
+    m, A = cpu_sample(args.config, args.seed, 0.12)      # ~0.12 s of CPU work per step
+    for _ in range(args.warmup):
+        cpu_ref.cpu_qr(A)
+    t = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        cpu_ref.cpu_qr(A)
+        t.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.mean(t)
+    value = m / (ms / 1e3)
+    sample = (f"torch.linalg.qr (LAPACK sgeqrf+sorgqr, fp32) on {m} of the {batch} {args.config} "
+              f"matrices per step, {threads} host threads")
+    return {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "matrices/s",
+        "gflops": value * flops_per_matrix(n) / 1e9, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded",
+        "config": {"workload": args.config, "batch": batch, "n": n, "sample_matrices": m},
+        "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": threads, "kind": "reference",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_ours(args) -> dict | None:
+    import qr_b200
+    from qr_b200.inputs import CONFIGS, config_input
+
+    dist, rank, world, local = dist_init(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    batch, n, kind = CONFIGS[args.config]
+    A = config_input(args.config, seed=args.seed + rank, device=dev)
+    H = torch.empty_like(A)
+    tau = torch.empty(batch, n, device=dev)
+    Q = torch.empty_like(A)
+    flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        qr_b200.qr(A, out=(H, tau, Q))
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier(dist, dev)
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clocks:
+        barrier(dist, dev)
+        for i in range(args.steps):
+            flush.fill_(42)                      # L2 flush, outside the events
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        barrier(dist, dev)
+    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_local = statistics.mean(times)
+    ms = reduce_max(dist, ms_local, dev)
+
+    # end to end through the public API: pinned host A -> device, QR, H/tau/Q -> pinned host
+    e2e = None
+    if not args.no_e2e:
+        A_h = A.cpu().pin_memory()
+        H_h = torch.empty(H.shape, dtype=H.dtype).pin_memory()
+        t_h = torch.empty(tau.shape, dtype=tau.dtype).pin_memory()
+        Q_h = torch.empty(Q.shape, dtype=Q.dtype).pin_memory()
+
+        def e2e_step():
+            a = A_h.to(dev, non_blocking=True)
+            h, t, q = qr_b200.qr(a)
+            H_h.copy_(h, non_blocking=True)
+            t_h.copy_(t, non_blocking=True)
+            Q_h.copy_(q, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        barrier(dist, dev)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k_e2e = max(3, min(args.steps, 20))
+        ev0.record(stream)
+        for _ in range(k_e2e):
+            e2e_step()
+        ev1.record(stream)
+        barrier(dist, dev)
+        ms_e2e = reduce_max(dist, ev0.elapsed_time(ev1) / k_e2e, dev)
+        h2d = A.numel() * 4
+        d2h = (H.numel() + tau.numel() + Q.numel()) * 4
+        e2e = {"value": world * batch / (ms_e2e / 1e3), "unit": "matrices/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
+               "steps": k_e2e, "api": "qr_b200.qr (C ABI qrb_qr_f32)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(args.config, args.seed)
+
+    if rank != 0:
+        return None
+    peaks = load_peaks()
+    value = world * batch / (ms / 1e3)
+    alg_bytes = batch * bytes_per_matrix(n)
+    kdur_s = ms_local / 1e3 if kernel_launches(n) == 1 else None
+    roof = None
+    if kdur_s is not None:
+        ach = alg_bytes / kdur_s / 1e9
+        traffic = load_traffic(args.config)
+        roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": ach / peaks["hbm_gbs"], "traffic": traffic, "kernel": dominant_kernel(n),
+                "algorithmic_bytes_per_launch": alg_bytes,
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"}
+    return {
+        "metric": METRIC, "value": value, "unit": "matrices/s",
+        "gflops": value * flops_per_matrix(n) / 1e9, "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded per rank",
+        "config": {"workload": args.config, "batch_per_gpu": batch, "n": n, "global_batch": world * batch,
+                   "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed between steps (256 MiB write)",
+                   "op": "geqrf + orgqr (qrb_qr_f32)"},
+        "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
+        "gpu_launches": kernel_launches(n) * args.steps,
+        "clocks": clocks.summary(),
+    }
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args(argv)
+    out = run_reference(args) if args.impl == "reference" else run_ours(args)
+    if out is not None:
+        print(json.dumps(out), flush=True)
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        import torch.distributed as dist
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,89 @@
+/*
+ * qrb200.h -- C ABI of the B200-native batched Householder QR library (libqrb200.so).
+ *
+ * Drop-in boundary for the reference's submission entry point
+ *   custom_kernel(data: Tensor[batch, n, n] f32 cuda) -> (H, tau)
+ * (submission.py:913-921; contract in reference_repo/task.yml:12-27 and
+ * reference_repo/task.py:4-5) and for the Q formation its checker performs with
+ * torch.linalg.householder_product (reference_repo/reference.py:144).
+ *
+ * Conventions for every entry point:
+ *   - Matrices are dense, row-major, contiguous (batch, n, n) fp32 in device memory,
+ *     exactly the layout reference.generate_input returns (reference.py:87).
+ *   - (H, tau) follow torch.geqrf / LAPACK SGEQRF compact form: R in the upper
+ *     triangle of H, unit-leading Householder vectors strictly below the diagonal,
+ *     tau[batch, n]; reflector convention of submissions/v1.py:9-38
+ *     (beta = -sign(alpha)*||x||, sign(0) = +1).
+ *   - All work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream) and is asynchronous with respect to the host.  The library never
+ *     allocates device memory on these paths; scratch comes from the caller's
+ *     `workspace` of at least qrb_workspace_size() bytes (256-byte aligned).
+ *   - Return value is a qrb_status.  Errors never throw; a per-thread message is
+ *     available from qrb_last_error().  Calls on distinct streams are independent;
+ *     one workspace must not be shared by calls that may run concurrently.
+ *   - A may alias H (in-place factorisation).  Q must not alias A, H or tau.
+ */
+#ifndef QRB200_H
+#define QRB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QRB_API __attribute__((visibility("default")))
+#else
+#define QRB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum qrb_status {
+  QRB_OK = 0,
+  QRB_ERR_INVALID_ARG = 1,   /* null pointer, n < 1, batch < 0, misaligned pointer */
+  QRB_ERR_UNSUPPORTED = 2,   /* n above QRB_MAX_N */
+  QRB_ERR_WORKSPACE = 3,     /* workspace missing or smaller than qrb_workspace_size() */
+  QRB_ERR_CUDA = 4,          /* a CUDA runtime call or kernel launch failed */
+  QRB_ERR_DEVICE = 5         /* current device is not an sm_100 (B200-class) GPU */
+};
+
+#define QRB_MAX_N 4096
+
+/* Library version, major*10000 + minor*100 + patch. */
+QRB_API int qrb_version(void);
+
+/* Static description of a status code. */
+QRB_API const char* qrb_status_string(int status);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len).  Returns the status of the last failing call on this thread
+ * (QRB_OK if none). */
+QRB_API int qrb_last_error(char* buf, size_t len);
+
+/* Bytes of device workspace the calls below need for (batch, n).  0 is a valid
+ * answer (small n needs none).  Same value for geqrf, orgqr and qr. */
+QRB_API size_t qrb_workspace_size(int64_t batch, int n);
+
+/* Batched Householder QR in compact form:  (H, tau) = geqrf(A).
+ * Replaces custom_kernel (submission.py:913-921) / ref_kernel's torch.geqrf
+ * (reference_repo/reference.py:90-92).  A is not modified unless A == H. */
+QRB_API int qrb_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int n,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Q = H_0 H_1 ... H_{n-1} from compact (H, tau) (the full n x n orthogonal factor).
+ * Replaces torch.linalg.householder_product(H, tau) (reference_repo/reference.py:144). */
+QRB_API int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int n,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused full QR: (H, tau) = geqrf(A) and Q = householder_product(H, tau) in one call,
+ * reusing the block reflector factors between the two phases.  R = triu(H).
+ * The north-star path: torch.linalg.qr(A) with Q and R both available. */
+QRB_API int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRB200_H */

@@ -1,0 +1,211 @@
+// C ABI of libqrb200 (declared in include/qrb200.h): argument checks, workspace
+// layout and the regime dispatch of the batched QR.
+//
+// Dispatch (replaces custom_kernel's shape dispatch, submission.py:905-921):
+//   n <= 64  : one fused CTA per matrix (qrb_small.cu) -- geqrf and Q in one launch.
+//   n >  64  : right-looking blocked Householder, panel width 32:
+//                for each panel k: panel geqr2 + T (qrb_panel.cu), then the
+//                trailing update A[k:, k+32:] -= V T^T V^T A (qrb_apply.cu);
+//              Q by backward block accumulation Q[k:, k:] -= V T V^T Q[k:, k:]
+//              over the same T factors, with the identity generated on the fly.
+// Workspace: the T factors of every panel, [panel][batch][32][32] fp32.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "../../include/qrb200.h"
+#include "qrb_internal.cuh"
+
+namespace {
+
+thread_local std::string g_last_msg;
+thread_local int g_last_status = QRB_OK;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_last_msg = buf;
+  g_last_status = status;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(QRB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int n_panels(int n) { return (n + qrb::kNB - 1) / qrb::kNB; }
+
+size_t ws_bytes(int64_t batch, int n) {
+  if (n <= qrb::kSmallMaxN) return 0;
+  return (size_t)n_panels(n) * (size_t)batch * qrb::kNB * qrb::kNB * sizeof(float);
+}
+
+// The kernels are built for sm_100a only: refuse anything else up front rather
+// than failing with "no kernel image" deep inside a launch sequence.
+int check_device() {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  static int major_cache[64] = {0};
+  int major = dev < 64 ? major_cache[dev] : 0;
+  if (major == 0) {
+    e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    if (dev < 64) major_cache[dev] = major;
+  }
+  if (major != 10) return fail(QRB_ERR_DEVICE, "device %d has compute capability %d.x; libqrb200 needs sm_100", dev, major);
+  return QRB_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_common(int64_t batch, int n, const void* ws, size_t wsb) {
+  if (batch < 0) return fail(QRB_ERR_INVALID_ARG, "batch must be >= 0 (got %lld)", (long long)batch);
+  if (n < 1) return fail(QRB_ERR_INVALID_ARG, "n must be >= 1 (got %d)", n);
+  if (n > QRB_MAX_N) return fail(QRB_ERR_UNSUPPORTED, "n = %d exceeds QRB_MAX_N = %d", n, QRB_MAX_N);
+  if (batch > (int64_t)1 << 31) return fail(QRB_ERR_UNSUPPORTED, "batch = %lld exceeds 2^31", (long long)batch);
+  const size_t need = ws_bytes(batch, n);
+  if (need > 0 && (ws == nullptr || wsb < need))
+    return fail(QRB_ERR_WORKSPACE, "workspace of %zu bytes required, %zu given%s", need, wsb,
+                ws == nullptr ? " (null)" : "");
+  if (need > 0 && (reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+    return fail(QRB_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  return QRB_OK;
+}
+
+// Matrices are read and written with 16-byte vector accesses; tau only needs float alignment.
+int check_ptr(const void* p, const char* name, bool vec = true) {
+  if (p == nullptr) return fail(QRB_ERR_INVALID_ARG, "%s is null", name);
+  if (vec ? !aligned16(p) : (reinterpret_cast<uintptr_t>(p) & 3u) != 0)
+    return fail(QRB_ERR_INVALID_ARG, "%s must be %d-byte aligned", name, vec ? 16 : 4);
+  return QRB_OK;
+}
+
+#define QRB_TRY(x)                   \
+  do {                               \
+    int _s = (x);                    \
+    if (_s != QRB_OK) return _s;     \
+  } while (0)
+#define QRB_CUDA(x, what)                          \
+  do {                                             \
+    cudaError_t _e = (x);                          \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+float* panel_T(void* ws, int64_t batch, int p) {
+  return static_cast<float*>(ws) + (size_t)p * (size_t)batch * qrb::kNB * qrb::kNB;
+}
+
+int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, void* ws,
+                  cudaStream_t s) {
+  const int np = n_panels(n);
+  for (int p = 0; p < np; ++p) {
+    const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
+    const float* src = p == 0 ? A : H;
+    float* T = panel_T(ws, batch, p);
+    QRB_CUDA(qrb::launch_panel(src, H, tau, T, batch, n, k, b, s), "panel kernel launch");
+    if (k + b < n)
+      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, s), "trailing update launch");
+  }
+  return QRB_OK;
+}
+
+int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  for (int p = n_panels(n) - 1; p >= 0; --p) {
+    const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
+    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, s),
+             "orgqr block launch");
+  }
+  return QRB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qrb_version(void) { return 100; }
+
+const char* qrb_status_string(int status) {
+  switch (status) {
+    case QRB_OK: return "ok";
+    case QRB_ERR_INVALID_ARG: return "invalid argument";
+    case QRB_ERR_UNSUPPORTED: return "unsupported size";
+    case QRB_ERR_WORKSPACE: return "workspace missing or too small";
+    case QRB_ERR_CUDA: return "CUDA error";
+    case QRB_ERR_DEVICE: return "unsupported device";
+    default: return "unknown status";
+  }
+}
+
+int qrb_last_error(char* buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    std::strncpy(buf, g_last_msg.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return g_last_status;
+}
+
+size_t qrb_workspace_size(int64_t batch, int n) {
+  if (batch < 0 || n < 1 || n > QRB_MAX_N) return 0;
+  return ws_bytes(batch, n);
+}
+
+int qrb_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int n, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  QRB_TRY(check_ptr(A, "A"));
+  QRB_TRY(check_ptr(H, "H"));
+  QRB_TRY(check_ptr(tau, "tau", false));
+  if (batch == 0) return QRB_OK;
+  QRB_TRY(check_device());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n <= qrb::kSmallMaxN) {
+    QRB_CUDA(qrb::launch_small(A, H, tau, nullptr, batch, n, 1, s), "small-n kernel launch");
+    return QRB_OK;
+  }
+  return blocked_geqrf(A, H, tau, batch, n, workspace, s);
+}
+
+int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int n,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+  QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  QRB_TRY(check_ptr(H, "H"));
+  QRB_TRY(check_ptr(tau, "tau", false));
+  QRB_TRY(check_ptr(Q, "Q"));
+  if (Q == H) return fail(QRB_ERR_INVALID_ARG, "Q must not alias H");
+  if (batch == 0) return QRB_OK;
+  QRB_TRY(check_device());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n <= qrb::kSmallMaxN) {
+    QRB_CUDA(qrb::launch_small(nullptr, const_cast<float*>(H), const_cast<float*>(tau), Q, batch, n, 2, s),
+             "small-n kernel launch");
+    return QRB_OK;
+  }
+  QRB_CUDA(qrb::launch_larft(H, tau, static_cast<float*>(workspace), batch, n, s), "larft launch");
+  return blocked_orgqr(H, Q, batch, n, workspace, s);
+}
+
+int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
+               void* workspace, size_t workspace_bytes, void* stream) {
+  QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  QRB_TRY(check_ptr(A, "A"));
+  QRB_TRY(check_ptr(H, "H"));
+  QRB_TRY(check_ptr(tau, "tau", false));
+  QRB_TRY(check_ptr(Q, "Q"));
+  if (Q == H || Q == A) return fail(QRB_ERR_INVALID_ARG, "Q must not alias A or H");
+  if (batch == 0) return QRB_OK;
+  QRB_TRY(check_device());
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n <= qrb::kSmallMaxN) {
+    QRB_CUDA(qrb::launch_small(A, H, tau, Q, batch, n, 3, s), "small-n kernel launch");
+    return QRB_OK;
+  }
+  QRB_TRY(blocked_geqrf(A, H, tau, batch, n, workspace, s));
+  return blocked_orgqr(H, Q, batch, n, workspace, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// Internal declarations shared by the libqrb200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qrb {
+
+// Panel (block reflector) width of the blocked path.  Every panel is factored
+// by one lane-per-column kernel, so the width is the warp size.
+constexpr int kNB = 32;
+
+// Matrices with n <= kSmallMaxN are factored (and Q formed) by one CTA each,
+// entirely on chip.
+constexpr int kSmallMaxN = 64;
+
+// Reflector convention of submissions/v1.py:9-38: |v0| below this is replaced by 1.
+constexpr float kEpsV0 = 1e-30f;
+
+// ---- device helpers --------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Householder reflector from alpha = x[0] and tail2 = ||x[1:]||^2, following
+// submissions/v1.py:17-29: beta = -sign(alpha)*||x|| (sign(0) = +1),
+// v0 = alpha - beta, tau = 2 v0^2 / (v0^2 + tail2) (0 if that is 0),
+// u = x[1:] * (1 / v0) with |v0| < 1e-30 -> v0 := 1.
+struct Reflector {
+  float beta, tau, inv_v0;
+};
+
+__device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bool trivial) {
+  Reflector r;
+  if (trivial) {  // m == 1: H = I (v1.py:14-16)
+    r.beta = alpha;
+    r.tau = 0.f;
+    r.inv_v0 = 1.f;
+    return r;
+  }
+  float norm = sqrtf(alpha * alpha + tail2);
+  float beta = alpha >= 0.f ? -norm : norm;
+  float v0 = alpha - beta;
+  float vn2 = v0 * v0 + tail2;
+  r.beta = beta;
+  r.tau = vn2 > 0.f ? (2.f * v0 * v0) / vn2 : 0.f;
+  r.inv_v0 = 1.f / (fabsf(v0) < kEpsV0 ? 1.f : v0);
+  return r;
+}
+
+// ---- launchers (return cudaError_t of the launch) ---------------------------
+// Small-n fused kernel: geqrf and/or orgqr of n <= 64 matrices, one CTA each.
+// mode bit 0: factor A -> (H, tau); bit 1: form Q from (H, tau).
+cudaError_t launch_small(const float* A, float* H, float* tau, float* Q,
+                         int64_t batch, int n, int mode, cudaStream_t s);
+
+// Panel factorisation of H[:, k:, k:k+b] (b <= 32) with T factor:
+// reads the panel from `src` (A on the first panel, otherwise H), writes the
+// factored panel to H, tau[:, k:k+b] and T[batch][32][32] (upper triangular,
+// I - V T V^T = H_k ... H_{k+b-1}).
+cudaError_t launch_panel(const float* src, float* H, float* tau, float* T,
+                         int64_t batch, int n, int k, int b, cudaStream_t s);
+
+// Block reflector application  C[:, k:, c0:] -= V op(T) (V^T C[:, k:, c0:])
+// with V = unit-lower reflectors H[:, k:, k:k+b].  trans_t = 1 applies T^T
+// (Q_k^T, the geqrf trailing update), 0 applies T (Q_k, orgqr).  `src` is read
+// (it may equal C).  If identity_fill, entries of C with row < k+b or column < k+b
+// are taken as the identity instead of being read (orgqr without a Q init).
+cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
+                         int64_t batch, int n, int k, int b, int c0, int trans_t,
+                         int identity_fill, cudaStream_t s);
+
+// T factors of all panels from (H, tau), for orgqr without a preceding geqrf.
+cudaError_t launch_larft(const float* H, const float* tau, float* T_all,
+                         int64_t batch, int n, cudaStream_t s);
+
+}  // namespace qrb

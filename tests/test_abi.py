@@ -1,0 +1,101 @@
+"""CPU: the C-ABI library loads, exports what include/qrb200.h declares, and
+validates arguments on the host before touching a device."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = ROOT / "include" / "qrb200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build  # linalg-gpu-comp_b200/build.py
+    build.build()
+    from qr_b200 import _lib
+    return _lib.lib()
+
+
+def declared_symbols():
+    text = HEADER.read_text()
+    return re.findall(r"QRB_API\s+[\w\s\*]+?\b(qrb_\w+)\s*\(", text)
+
+
+def test_header_declares_the_api():
+    assert set(declared_symbols()) == {
+        "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
+        "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32"}
+
+
+def test_library_exports_every_declared_symbol(lib):
+    from qr_b200 import _lib
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, name
+
+
+def test_version_and_status_strings(lib):
+    assert lib.qrb_version() >= 100
+    assert lib.qrb_status_string(0) == b"ok"
+    assert b"workspace" in lib.qrb_status_string(3)
+    assert lib.qrb_status_string(99) == b"unknown status"
+
+
+@pytest.mark.parametrize("batch,n,expect", [
+    (10, 1, 0), (10, 64, 0), (10, 65, 3 * 10 * 32 * 32 * 4), (7, 512, 16 * 7 * 4096),
+    (32, 2048, 64 * 32 * 4096), (1, 4097, 0), (-1, 100, 0)])
+def test_workspace_size(lib, batch, n, expect):
+    assert lib.qrb_workspace_size(batch, n) == expect
+
+
+def _err(lib):
+    buf = ctypes.create_string_buffer(256)
+    st = lib.qrb_last_error(buf, 256)
+    return st, buf.value.decode()
+
+
+FAKE = 0x10000  # a 256-byte aligned non-null address; never dereferenced (checks fail first or batch == 0)
+
+
+def test_argument_errors_are_statuses(lib):
+    # null pointers
+    assert lib.qrb_geqrf_f32(None, FAKE, FAKE, 4, 32, None, 0, None) == 1
+    assert "A is null" in _err(lib)[1]
+    assert lib.qrb_qr_f32(FAKE, FAKE, FAKE, None, 4, 32, None, 0, None) == 1
+    # bad sizes
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 0, None, 0, None) == 1
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, -1, 8, None, 0, None) == 1
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 5000, None, 0, None) == 2
+    assert "QRB_MAX_N" in _err(lib)[1]
+    # workspace
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 128, None, 0, None) == 3
+    assert lib.qrb_orgqr_f32(FAKE, FAKE, FAKE + 256, 4, 128, FAKE, 16, None) == 3
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 128, FAKE + 16, 1 << 20, None) == 1
+    # alignment of matrices
+    assert lib.qrb_geqrf_f32(FAKE + 4, FAKE, FAKE, 4, 32, None, 0, None) == 1
+    assert "aligned" in _err(lib)[1]
+    # aliasing
+    assert lib.qrb_qr_f32(FAKE, FAKE, FAKE, FAKE, 4, 32, None, 0, None) == 1
+    assert lib.qrb_orgqr_f32(FAKE, FAKE, FAKE, 4, 32, None, 0, None) == 1
+    st, msg = _err(lib)
+    assert st == 1 and "alias" in msg
+
+
+def test_empty_batch_is_a_no_op(lib):
+    # batch == 0 returns before any CUDA call, so it succeeds without a device.
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 0, 32, None, 0, None) == 0
+    assert lib.qrb_qr_f32(FAKE, FAKE, FAKE, FAKE + 256, 0, 300, None, 0, None) == 0
+
+
+def test_python_ops_reject_cpu_and_wrong_dtype():
+    import torch
+    from qr_b200 import custom_kernel, form_q
+    with pytest.raises(ValueError, match="CUDA"):
+        custom_kernel(torch.randn(2, 8, 8))
+    with pytest.raises(TypeError):
+        custom_kernel(torch.randn(2, 8, 8, dtype=torch.float64).to("meta"))
+    with pytest.raises(ValueError):
+        form_q(torch.randn(2, 8, 8), torch.randn(2, 8))

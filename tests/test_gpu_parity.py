@@ -1,0 +1,248 @@
+"""GPU parity: libqrb200 (through its C ABI, via the qr_b200 ctypes shim) against
+the CPU oracle, the reference's golden outputs and the reference's checker.
+
+Tolerances (fp32 arithmetic, different summation order than the reference):
+  * H vs the reference's v1 output: max |dH| <= 5e-5 * max|A|, max |dtau| <= 5e-5
+    (well-determined cases; rank-deficient tails are checked by properties only);
+  * reference gate (reference_repo/reference.py:127-192): must pass;
+  * north-star measures: ||QR - A||_F/||A||_F <= 1e-5, spectral ||Q^T Q - I|| <= 1e-5,
+    sign-normalised R vs torch.linalg.qr's R <= 1e-4 (relative Frobenius).
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_cases
+from oracle import qr_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL_H = 5e-5
+TOL_RECON = 1e-5
+TOL_ORTH = 1e-5
+TOL_R = 1e-4
+DEGENERATE = {"nearrank", "nearcollinear"}
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import build
+    build.build()
+    torch.cuda.init()
+
+
+def qrb():
+    import qr_b200
+    return qr_b200
+
+
+# ---------------------------------------------------------------------------
+# checkers (fp64, on the device)
+# ---------------------------------------------------------------------------
+def reference_gate(A, H, tau):
+    """torch restatement of reference.check_implementation (reference.py:127-192)."""
+    n = A.shape[-1]
+    eps = torch.finfo(torch.float32).eps
+    q = torch.linalg.householder_product(H, tau).double()
+    r = torch.triu(H).double()
+    a = A.double()
+    l1 = lambda x: torch.linalg.matrix_norm(x, ord=1, dim=(-2, -1))
+    proj = q.transpose(-1, -2) @ a
+    f_res = l1(r - proj).amax().item()
+    f_ok = f_res <= 20.0 * n * eps * l1(a).amax().item()
+    eye = torch.eye(n, device=A.device, dtype=torch.float64)
+    o_res = l1(q.transpose(-1, -2) @ q - eye).amax().item()
+    o_ok = o_res <= 100.0 * n * eps
+    return f_ok and o_ok and bool(torch.isfinite(H).all()) and bool(torch.isfinite(tau).all()), (f_res, o_res)
+
+
+def north_star(A, Q, R, R_ref=None):
+    a, q, r = A.double(), Q.double(), R.double()
+    n = A.shape[-1]
+    recon = (torch.linalg.matrix_norm(q @ r - a) / torch.linalg.matrix_norm(a).clamp_min(1e-300)).amax().item()
+    e = q.transpose(-1, -2) @ q - torch.eye(n, device=A.device, dtype=torch.float64)
+    orth = torch.linalg.eigvalsh(e).abs().amax().item()
+    out = {"recon": recon, "orth": orth}
+    if R_ref is not None:
+        rr = R_ref.double()
+        s = torch.where(torch.diagonal(r, dim1=-2, dim2=-1) >= 0, 1.0, -1.0).unsqueeze(-1)
+        s2 = torch.where(torch.diagonal(rr, dim1=-2, dim2=-1) >= 0, 1.0, -1.0).unsqueeze(-1)
+        out["rdiff"] = (torch.linalg.matrix_norm(s * r - s2 * rr) /
+                        torch.linalg.matrix_norm(rr).clamp_min(1e-300)).amax().item()
+    return out
+
+
+def assert_north_star(A, H, Q, tol_r=TOL_R):
+    R = torch.triu(H)
+    _, R_ref = torch.linalg.qr(A)
+    m = north_star(A, Q, R, R_ref)
+    assert m["recon"] <= TOL_RECON, m
+    assert m["orth"] <= TOL_ORTH, m
+    assert m["rdiff"] <= tol_r, m
+    return m
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures (reference outputs)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("name,case", golden_cases())
+def test_golden_geqrf(golden, name, case):
+    A_np = golden[f"{name}/A"]
+    A = torch.from_numpy(A_np).cuda()
+    H, tau = qrb().custom_kernel(A)
+    torch.cuda.synchronize()
+    Hn, tn = H.cpu().numpy(), tau.cpu().numpy()
+    ok, info = O.check_implementation(A_np, Hn, tn)
+    assert ok, info
+    if case not in DEGENERATE:
+        scale = np.abs(A_np).max() + 1e-30
+        assert np.abs(Hn - golden[f"{name}/H_v1"]).max() <= TOL_H * scale
+        assert np.abs(tn - golden[f"{name}/tau_v1"]).max() <= TOL_H
+        H64, t64 = O.geqr2(A_np)
+        assert np.abs(Hn - H64).max() <= TOL_H * scale
+
+
+@pytest.mark.parametrize("name,case", golden_cases())
+def test_golden_qr_q_matches_oracle(golden, name, case):
+    A = torch.from_numpy(golden[f"{name}/A"]).cuda()
+    H, tau, Q = qrb().qr(A)
+    H1, tau1 = qrb().custom_kernel(A)
+    torch.cuda.synchronize()
+    assert torch.equal(H, H1) and torch.equal(tau, tau1)
+    Q_or = O.orgqr(H.cpu().numpy(), tau.cpu().numpy())
+    assert np.abs(Q.cpu().numpy() - Q_or).max() <= 2e-6
+
+
+# ---------------------------------------------------------------------------
+# sizes: every regime boundary, ragged n, tiny batches
+# ---------------------------------------------------------------------------
+SIZES = [1, 2, 3, 4, 5, 7, 8, 15, 16, 17, 31, 32, 33, 47, 63, 64, 65, 66, 95, 96, 97,
+         127, 128, 129, 176, 200, 255, 256, 257, 352, 511, 512, 513, 700]
+
+
+@pytest.mark.parametrize("n", SIZES)
+def test_sizes_qr(n):
+    g = torch.Generator(device="cuda").manual_seed(1000 + n)
+    batch = 3 if n <= 256 else 2
+    A = torch.randn(batch, n, n, device="cuda", generator=g)
+    H, tau, Q = qrb().qr(A)
+    ok, res = reference_gate(A, H, tau)
+    assert ok, res
+    assert_north_star(A, H, Q)
+    Q2 = qrb().form_q(H, tau)
+    assert (Q2 - Q).abs().max().item() <= 1e-5
+
+
+@pytest.mark.parametrize("n", [33, 64, 96, 130, 300])
+def test_matches_oracle_at_small_sizes(n):
+    A_np = np.random.default_rng(n).standard_normal((2, n, n)).astype(np.float32)
+    H, tau, Q = qrb().qr(torch.from_numpy(A_np).cuda())
+    H64, t64 = O.geqr2(A_np)
+    scale = np.abs(A_np).max()
+    assert np.abs(H.cpu().numpy() - H64).max() <= TOL_H * scale
+    assert np.abs(tau.cpu().numpy() - t64).max() <= TOL_H
+    assert np.abs(Q.cpu().numpy() - O.orgqr(H64, t64)).max() <= 2e-5
+
+
+# ---------------------------------------------------------------------------
+# the reference harness's structured cases and its task.yml test specs
+# ---------------------------------------------------------------------------
+CASES = ["dense", "upper", "diagonal", "rankdef", "nearrank", "clustered", "band",
+         "nearcollinear", "rowscale"]
+
+
+@pytest.mark.parametrize("n", [32, 64, 176, 512])
+@pytest.mark.parametrize("case", CASES)
+def test_structured_cases(case, n):
+    from qr_b200.inputs import task_input
+    A = task_input(2, n, 2 if case == "dense" else 0, 500 + n, case)
+    H, tau = qrb().custom_kernel(A)
+    ok, res = reference_gate(A, H, tau)
+    assert ok, (case, n, res)
+
+
+# reference_repo/task.yml:72-91 (batch, n, cond, seed, case)
+TASK_TESTS = [
+    (20, 32, 1, 53124, "dense"), (40, 176, 1, 3321, "dense"), (40, 352, 1, 1200, "dense"),
+    (16, 512, 2, 32523, "dense"), (4, 1024, 2, 4327, "dense"), (1, 4096, 1, 75342, "dense"),
+    (16, 512, 4, 32524, "dense"), (16, 512, 0, 32525, "rankdef"), (16, 512, 0, 32526, "clustered"),
+    (16, 512, 0, 32527, "band"), (16, 512, 0, 32528, "rowscale"), (16, 512, 0, 32529, "nearcollinear"),
+    (4, 1024, 4, 4328, "dense"), (4, 1024, 0, 4329, "rankdef"), (4, 1024, 0, 4330, "nearrank"),
+    (4, 1024, 0, 4331, "clustered"), (2, 2048, 2, 224466, "dense"), (2, 2048, 0, 224467, "rankdef"),
+    (1, 4096, 0, 75343, "upper"),
+]
+
+
+@pytest.mark.parametrize("spec", TASK_TESTS, ids=lambda s: f"b{s[0]}_n{s[1]}_{s[4]}_c{s[2]}")
+def test_task_yml_specs(spec):
+    from qr_b200.inputs import task_input
+    batch, n, cond, seed, case = spec
+    A = task_input(batch, n, cond, seed, case)
+    A_copy = A.clone()
+    H, tau = qrb().custom_kernel(A)
+    assert torch.equal(A, A_copy), "input was modified"
+    ok, res = reference_gate(A, H, tau)
+    assert ok, res
+
+
+# ---------------------------------------------------------------------------
+# the five benchmark configurations at full size: the north-star gate
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("config", ["b64_n32", "b4096_n64", "b512_n256", "b32_n2048",
+                                    "b256_n512_illcond"])
+def test_configs_north_star(config):
+    from qr_b200.inputs import config_input
+    A = config_input(config, seed=7)
+    H, tau, Q = qrb().qr(A)
+    m = assert_north_star(A, H, Q)
+    ok, res = reference_gate(A[:64], H[:64], tau[:64])
+    assert ok, res
+    print(config, m)
+
+
+# ---------------------------------------------------------------------------
+# boundary semantics
+# ---------------------------------------------------------------------------
+def test_in_place_and_streams():
+    from qr_b200 import _lib
+    for n in (48, 200):
+        A = torch.randn(4, n, n, device="cuda")
+        H_ref, tau_ref = qrb().custom_kernel(A)
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            H, tau = qrb().custom_kernel(A)      # on a side stream
+        s.synchronize()
+        assert torch.equal(H, H_ref) and torch.equal(tau, tau_ref)
+        # in place through the C ABI: A == H
+        X = A.clone()
+        t = torch.empty(4, n, device="cuda")
+        nb = _lib.lib().qrb_workspace_size(4, n)
+        ws = torch.empty(max(nb, 1), dtype=torch.uint8, device="cuda")
+        st = _lib.lib().qrb_geqrf_f32(X.data_ptr(), X.data_ptr(), t.data_ptr(), 4, n,
+                                      ws.data_ptr(), nb, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        assert st == 0
+        assert torch.equal(X, H_ref) and torch.equal(t, tau_ref)
+
+
+def test_noncontiguous_and_empty():
+    A = torch.randn(3, 40, 40, device="cuda")
+    H, tau = qrb().custom_kernel(A.transpose(-1, -2))
+    H2, tau2 = qrb().custom_kernel(A.transpose(-1, -2).contiguous())
+    assert torch.equal(H, H2) and torch.equal(tau, tau2)
+    H0, t0 = qrb().custom_kernel(torch.empty(0, 100, 100, device="cuda"))
+    assert H0.shape == (0, 100, 100) and t0.shape == (0, 100)
+
+
+def test_workspace_too_small_is_reported():
+    from qr_b200 import _lib
+    A = torch.randn(2, 100, 100, device="cuda")
+    H = torch.empty_like(A)
+    t = torch.empty(2, 100, device="cuda")
+    st = _lib.lib().qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), t.data_ptr(), 2, 100, None, 0,
+                                  torch.cuda.current_stream().cuda_stream)
+    assert st == _lib.QRB_ERR_WORKSPACE
