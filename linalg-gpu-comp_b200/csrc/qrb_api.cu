@@ -157,10 +157,10 @@ size_t qrb_workspace_size(int64_t batch, int n) {
 int qrb_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int n, void* workspace,
                   size_t workspace_bytes, void* stream) {
   QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  if (batch == 0) return QRB_OK;   // nothing to do; pointers may be null
   QRB_TRY(check_ptr(A, "A"));
   QRB_TRY(check_ptr(H, "H"));
   QRB_TRY(check_ptr(tau, "tau", false));
-  if (batch == 0) return QRB_OK;
   QRB_TRY(check_device());
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n <= qrb::kSmallMaxN) {
@@ -173,6 +173,7 @@ int qrb_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int n, vo
 int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int n,
                   void* workspace, size_t workspace_bytes, void* stream) {
   QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  if (batch == 0) return QRB_OK;   // nothing to do; pointers may be null
   QRB_TRY(check_ptr(H, "H"));
   QRB_TRY(check_ptr(tau, "tau", false));
   QRB_TRY(check_ptr(Q, "Q"));
@@ -192,6 +193,7 @@ int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int
 int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
                void* workspace, size_t workspace_bytes, void* stream) {
   QRB_TRY(check_common(batch, n, workspace, workspace_bytes));
+  if (batch == 0) return QRB_OK;   // nothing to do; pointers may be null
   QRB_TRY(check_ptr(A, "A"));
   QRB_TRY(check_ptr(H, "H"));
   QRB_TRY(check_ptr(tau, "tau", false));

@@ -85,7 +85,14 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
       cluster.sync();
     }
     {
-      float2 p = lane < CL * kPanelWarps ? red_n[par][lane] : make_float2(0.f, 0.f);
+      // CL * 8 partials (up to 64): lane l folds slots l, l + 32, ... then a butterfly.
+      float2 p = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int q = lane; q < CL * kPanelWarps; q += 32) {
+        const float2 t = red_n[par][q];
+        p.x += t.x;
+        p.y += t.y;
+      }
       tail = warp_sum(p.x);
       alpha = warp_sum(p.y);
     }
