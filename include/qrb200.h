@@ -82,6 +82,17 @@ QRB_API int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t ba
 QRB_API int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* (H, tau) = geqrf(A) without any caller workspace, for callers that cannot
+ * allocate device memory (a plugin host that passes only raw input/output pointers,
+ * or a path that must not enter the allocator).  No counterpart in the reference.
+ * Scratch lives in an 8 MiB static device array that every GPU loading the library
+ * keeps until exit; for n > 64 the batch is limited to 2048 (QRB_ERR_UNSUPPORTED
+ * beyond).  All calls share that array: calls that may overlap on the GPU race.
+ * The first call on a device looks the array up and should come before any
+ * stream capture.  Returns a qrb_status; it does not set qrb_last_error. */
+QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch, int n,
+                                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

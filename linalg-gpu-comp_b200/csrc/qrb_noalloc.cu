@@ -1,0 +1,100 @@
+// qrb_geqrf_f32_noalloc: the compact QR factorisation for callers that cannot
+// allocate device memory.
+//
+// Some callers cannot call cudaMalloc at the point where they need a
+// factorisation: a plugin host or foreign runtime that hands the library only raw
+// input and output pointers and owns no device allocator, or a latency-critical
+// path that must not enter the allocator (cudaMalloc can synchronise the device)
+// and works within a memory budget reserved up front.  The regular entry point
+// needs a caller workspace for the per-panel T factors of the blocked path
+// (n > 64).  This variant keeps that scratch in a file-scope __device__ array
+// instead, so the caller passes only A, H and tau.
+//
+// Limits and sharing rules:
+//   * The scratch holds ONE panel's T factors for every matrix of the batch
+//     (32 x 32 fp32 = 4 KiB per matrix), so for n > 64 the batch may be at most
+//     kNoAllocScratchBytes / 4 KiB = 2048 matrices.  n <= 64 needs no scratch
+//     and has no batch limit.  Larger batches are rejected (QRB_ERR_UNSUPPORTED).
+//   * Every GPU that loads the library holds the 8 MiB array until process exit.
+//   * Every call shares the one array.  Each panel writes its T block in full
+//     before the trailing update reads it, so nothing has to be cleared between
+//     calls, but calls that may overlap on the GPU (different streams, or
+//     different host threads without ordering) race on the scratch.
+//   * The device address of the array is looked up once per device by the first
+//     call made with that device current (cudaGetSymbolAddress); make that first
+//     call before any stream capture begins.
+#include <atomic>
+#include <mutex>
+
+#include "../../include/qrb200.h"
+#include "qrb_internal.cuh"
+
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(8) << 20;   // 8 MiB
+constexpr size_t kTBytes = size_t(qrb::kNB) * qrb::kNB * sizeof(float);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::atomic<void*> g_scratch_ptr[kMaxDevices];
+std::mutex g_setup_mutex;
+
+// Device address of g_noalloc_scratch on the current device (looked up once).
+cudaError_t scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  void* p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    std::lock_guard<std::mutex> lock(g_setup_mutex);
+    p = g_scratch_ptr[dev].load(std::memory_order_acquire);
+    if (p == nullptr) {
+      e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+      if (e != cudaSuccess) return e;
+      g_scratch_ptr[dev].store(p, std::memory_order_release);
+    }
+  }
+  *out = p;
+  return cudaSuccess;
+}
+
+}  // namespace
+
+extern "C" QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch,
+                                             int n, void* stream) {
+  // Argument checks mirror qrb_geqrf_f32; the workspace is internal.
+  if (batch < 0 || n < 1) return QRB_ERR_INVALID_ARG;
+  if (n > QRB_MAX_N) return QRB_ERR_UNSUPPORTED;
+  if (batch == 0) return QRB_OK;
+  if (n > qrb::kSmallMaxN && (size_t)batch * kTBytes > kNoAllocScratchBytes) return QRB_ERR_UNSUPPORTED;
+  if (A == nullptr || H == nullptr || tau == nullptr) return QRB_ERR_INVALID_ARG;
+  if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(H) & 15u) ||
+      (reinterpret_cast<uintptr_t>(tau) & 3u))
+    return QRB_ERR_INVALID_ARG;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return QRB_ERR_CUDA;
+  if (major != 10) return QRB_ERR_DEVICE;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (n <= qrb::kSmallMaxN)
+    return qrb::launch_small(A, H, tau, nullptr, batch, n, 1, s) == cudaSuccess ? QRB_OK : QRB_ERR_CUDA;
+
+  void* scratch = nullptr;
+  if (scratch_address(&scratch) != cudaSuccess) return QRB_ERR_CUDA;
+  float* T = static_cast<float*>(scratch);
+  // Same right-looking blocked algorithm as qrb_geqrf_f32, with one T slot reused
+  // by every panel (stream order keeps panel p+1 from overwriting it early).
+  for (int k = 0; k < n; k += qrb::kNB) {
+    const int b = n - k < qrb::kNB ? n - k : qrb::kNB;
+    const float* src = k == 0 ? A : H;
+    if (qrb::launch_panel(src, H, tau, T, batch, n, k, b, s) != cudaSuccess) return QRB_ERR_CUDA;
+    if (k + b < n &&
+        qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, s) != cudaSuccess)
+      return QRB_ERR_CUDA;
+  }
+  return QRB_OK;
+}

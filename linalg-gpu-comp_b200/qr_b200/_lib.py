@@ -29,6 +29,7 @@ SIGNATURES = {
     "qrb_geqrf_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_orgqr_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_qr_f32": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
+    "qrb_geqrf_f32_noalloc": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp]),
 }
 
 _lock = threading.Lock()

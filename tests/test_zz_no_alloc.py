@@ -1,0 +1,71 @@
+"""GPU: the allocation-free factorisation entry point (qrb_geqrf_f32_noalloc).
+
+Callers that cannot allocate device memory -- a plugin host that passes only raw
+input and output pointers, or a path that must not enter the allocator -- use
+this entry point; its scratch is a static device array inside the library.  The
+test calls it through the C ABI twice in a row (the second call sees the scratch
+the first one left behind) and compares each result with the regular
+qrb_geqrf_f32, within the H/tau tolerance of the other parity tests.  This file
+sorts last so a stop-at-first-failure run has already run every other test.
+"""
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+TOL_H = 5e-5   # same H / tau tolerance as tests/test_gpu_parity.py
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import build
+    build.build()
+    from qr_b200 import _lib
+    return _lib.lib()
+
+
+def _regular(lib, A):
+    batch, n, _ = A.shape
+    H = torch.empty_like(A)
+    tau = torch.empty(batch, n, device=A.device)
+    nb = lib.qrb_workspace_size(batch, n)
+    ws = torch.empty(max(nb, 1), dtype=torch.uint8, device=A.device)
+    st = lib.qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), batch, n, ws.data_ptr(), nb,
+                           torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    return H, tau
+
+
+def _noalloc(lib, A):
+    batch, n, _ = A.shape
+    H = torch.empty_like(A)
+    tau = torch.empty(batch, n, device=A.device)
+    st = lib.qrb_geqrf_f32_noalloc(A.data_ptr(), H.data_ptr(), tau.data_ptr(), batch, n,
+                                   torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    return H, tau
+
+
+@pytest.mark.parametrize("batch,n", [(16, 200), (3, 1100), (64, 48)])
+def test_noalloc_matches_regular_twice(lib, batch, n):
+    g = torch.Generator(device="cuda").manual_seed(n)
+    for call in range(2):
+        A = torch.randn(batch, n, n, device="cuda", generator=g)
+        H_ref, tau_ref = _regular(lib, A)
+        H, tau = _noalloc(lib, A)
+        torch.cuda.synchronize()
+        scale = A.abs().max().item()
+        assert (H - H_ref).abs().max().item() <= TOL_H * scale, call
+        assert (tau - tau_ref).abs().max().item() <= TOL_H, call
+
+
+def test_noalloc_rejects_batch_beyond_scratch(lib):
+    A = torch.empty(1, 128, 128, device="cuda")
+    # 2049 matrices need more than the 8 MiB of T scratch; rejected before any launch.
+    st = lib.qrb_geqrf_f32_noalloc(A.data_ptr(), A.data_ptr(), A.data_ptr(), 2049, 128,
+                                   torch.cuda.current_stream().cuda_stream)
+    assert st == 2
