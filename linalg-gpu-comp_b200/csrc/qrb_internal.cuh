@@ -29,7 +29,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 // v0 = alpha - beta, tau = 2 v0^2 / (v0^2 + tail2) (0 if that is 0),
 // u = x[1:] * (1 / v0) with |v0| < 1e-30 -> v0 := 1.
 struct Reflector {
-  float beta, tau, inv_v0;
+  float beta, tau, inv_v0, v0;   // v0: the (guarded) pivot of the unscaled vector
 };
 
 __device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bool trivial) {
@@ -38,6 +38,7 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bo
     r.beta = alpha;
     r.tau = 0.f;
     r.inv_v0 = 1.f;
+    r.v0 = 1.f;
     return r;
   }
   float norm = sqrtf(alpha * alpha + tail2);
@@ -46,7 +47,8 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bo
   float vn2 = v0 * v0 + tail2;
   r.beta = beta;
   r.tau = vn2 > 0.f ? (2.f * v0 * v0) / vn2 : 0.f;
-  r.inv_v0 = 1.f / (fabsf(v0) < kEpsV0 ? 1.f : v0);
+  r.v0 = fabsf(v0) < kEpsV0 ? 1.f : v0;
+  r.inv_v0 = 1.f / r.v0;
   return r;
 }
 

@@ -6,201 +6,280 @@
 // step, and adds the Q formation its checker does with householder_product
 // (reference_repo/reference.py:144).
 //
-// Layout.  NP (32 or 64) is n rounded up.  The CTA has NP/16 warps; warp w owns
-// columns [16w, 16w+16).  Lane = 4*rg + cg (rg in 0..7, cg in 0..3) owns rows
-// {rg + 8i : i < NP/8} and columns {16w + 4cg + cc : cc < 4}, held in registers.
-// A column reduction over rows is then 8 partial sums in registers followed by a
-// 3-level xor shuffle across the 8 lanes sharing cg -- no shared memory and no
-// CTA barrier.  Only the pivot column's reflector crosses warps, through a
-// double-buffered shared vector, so geqrf costs one __syncthreads per column and
-// orgqr (backward accumulation, reflectors read from the H tile in shared memory)
-// needs none.  Warps whose columns are all left of the active column skip work.
+// Layout.  NP (32 or 64) is n rounded up.  Four lanes share a column: lane =
+// 8*rg + cl (rg in 0..3) of warp w owns column 8w + cl and the rows {rg + 4i}, all
+// in registers, so the CTA has NP/8 warps.  A column reduction over rows is a
+// register sum plus two xor shuffles (8, 16).
+//
+// Reflectors are published unscaled: u_j = (0.., v0, x_{j+1}, .., x_{n-1}) with
+// v0 = alpha - beta, so v = u / v0 and H_j = I - s_j u u^T with s_j = tau_j / v0^2.
+// The column owner writes u_j to shared memory once; consumers fold s_j into a
+// per-column coefficient, so no dynamic row index is needed in the update and
+// H's sub-diagonal is divided by v0 once at the end.
+//
+// geqrf step j: every warp still owning a column > j waits on one named barrier,
+// applies H_j to its columns (dot + update on the 16-row blocks that can be
+// non-zero, chosen at compile time from j / 16), and the warp owning column j+1
+// then forms ||x||^2 of that column (row predicates only in the one or two
+// blocks that straddle row j+1) and publishes u_{j+1}.
+// orgqr (backward accumulation) reads the stored u_j and needs no barrier.
 #include "qrb_internal.cuh"
 
 namespace qrb {
 namespace {
 
+constexpr int kRG = 4;            // lanes per column
+constexpr int kCW = 32 / kRG;     // columns per warp
+
 template <int NP>
 struct SmallCfg {
-  static constexpr int kWarps = NP / 16;
+  static constexpr int kWarps = NP / kCW;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kR = NP / 8;     // rows per thread
-  static constexpr int kLD = NP + 4;    // padded row stride of the shared tile (16 B aligned)
+  static constexpr int kR = NP / kRG;    // rows per lane
+  static constexpr int kB = kR / 4;      // float4 blocks per lane (4*kRG matrix rows each)
+  static constexpr int kBlockRows = 4 * kRG;
 };
 
-template <int NP>
-__device__ __forceinline__ void load_tile(float* tile, const float* __restrict__ g, int n) {
-  using C = SmallCfg<NP>;
-  const int tid = threadIdx.x;
-  if ((n & 3) == 0) {
-    const int n4 = n >> 2;
-    for (int idx = tid; idx < NP * (NP / 4); idx += C::kThreads) {
-      int r = idx / (NP / 4), c4 = idx % (NP / 4);
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (r < n && c4 < n4) v = __ldg(reinterpret_cast<const float4*>(g + (size_t)r * n) + c4);
-      *reinterpret_cast<float4*>(tile + r * C::kLD + 4 * c4) = v;
-    }
-  } else {
-    for (int idx = tid; idx < NP * NP; idx += C::kThreads) {
-      int r = idx / NP, c = idx % NP;
-      tile[r * C::kLD + c] = (r < n && c < n) ? __ldg(g + (size_t)r * n + c) : 0.f;
-    }
-  }
+__device__ __forceinline__ void named_barrier(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-template <int NP>
-__device__ __forceinline__ void store_tile(const float* tile, float* __restrict__ g, int n) {
-  using C = SmallCfg<NP>;
-  const int tid = threadIdx.x;
-  if ((n & 3) == 0) {
-    const int n4 = n >> 2;
-    for (int idx = tid; idx < n * n4; idx += C::kThreads) {
-      int r = idx / n4, c4 = idx % n4;
-      reinterpret_cast<float4*>(g + (size_t)r * n)[c4] =
-          *reinterpret_cast<const float4*>(tile + r * C::kLD + 4 * c4);
-    }
-  } else {
-    for (int idx = tid; idx < n * n; idx += C::kThreads) {
-      int r = idx / n, c = idx % n;
-      g[(size_t)r * n + c] = tile[r * C::kLD + c];
-    }
-  }
-}
-
-// Column-group reduction: sum over the 8 lanes that share cg (lane bits 2..4).
-__device__ __forceinline__ float rg_sum(float v) {
-  v += __shfl_xor_sync(0xffffffffu, v, 4);
+// Sum over the kRG lanes of a column (lane bits 3 and 4).
+__device__ __forceinline__ float col_sum(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 8);
   v += __shfl_xor_sync(0xffffffffu, v, 16);
   return v;
 }
 
+// Shared state: U[j][rg][b] = rows rg + kRG*(4b..4b+3) of u_j; S[j] = tau_j / v0_j^2.
 template <int NP>
-__global__ void __launch_bounds__(SmallCfg<NP>::kThreads)
+struct SmallSmem {
+  float4 U[NP][kRG][SmallCfg<NP>::kB];
+  float S[NP];
+};
+
+template <int NP>
+__device__ __forceinline__ int row_of(int rg, int i) { return rg + kRG * i; }
+
+// Write u_c (the calling lanes own column c) into U[c].  Blocks below B0 are zero,
+// blocks beyond B0+1 are copied as they are, the rest are masked by row.
+template <int NP, int B0>
+__device__ __forceinline__ void publish_u(SmallSmem<NP>& sm, const float (&a)[SmallCfg<NP>::kR],
+                                          int c, int rg, float v0) {
+  constexpr int kB = SmallCfg<NP>::kB;
+#pragma unroll
+  for (int b = 0; b < kB; ++b) {
+    float v[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int row = row_of<NP>(rg, 4 * b + q);
+      if (b < B0) v[q] = 0.f;
+      else if (b > B0 + 1) v[q] = a[4 * b + q];
+      else v[q] = row > c ? a[4 * b + q] : (row == c ? v0 : 0.f);
+    }
+    sm.U[c][rg][b] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+// Sum of squares of rows > c and the value at row c (c in blocks B0 or B0+1).
+template <int NP, int B0>
+__device__ __forceinline__ void column_stats(const float (&a)[SmallCfg<NP>::kR], int c, int rg,
+                                             float& tail, float& alpha) {
+  constexpr int kB = SmallCfg<NP>::kB;
+  float t0 = 0.f, t1 = 0.f;
+  alpha = 0.f;
+#pragma unroll
+  for (int b = B0; b < kB; ++b)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int row = row_of<NP>(rg, 4 * b + q);
+      const float x = a[4 * b + q];
+      if (b > B0 + 1) {
+        if (q & 1) t1 = fmaf(x, x, t1); else t0 = fmaf(x, x, t0);
+      } else {
+        t0 += row > c ? x * x : 0.f;
+        alpha += row == c ? x : 0.f;
+      }
+    }
+  tail = t0 + t1;
+}
+
+// One geqrf step: apply H_j (u_j, s_j) to this lane's column; if `pivot`, also
+// produce the reflector of column j+1 (owned by lanes with col == j+1).
+template <int NP, int B0>
+__device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[SmallCfg<NP>::kR], int j,
+                                           int n, int rg, int col, bool pivot, Reflector& mine) {
+  constexpr int kB = SmallCfg<NP>::kB;
+  float4 u[kB];
+#pragma unroll
+  for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
+  const float sj = sm.S[j];
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+  for (int b = B0; b < kB; ++b) {
+    d0 = fmaf(u[b].x, a[4 * b + 0], d0);
+    d1 = fmaf(u[b].y, a[4 * b + 1], d1);
+    d2 = fmaf(u[b].z, a[4 * b + 2], d2);
+    d3 = fmaf(u[b].w, a[4 * b + 3], d3);
+  }
+  const float d = col_sum((d0 + d1) + (d2 + d3));
+  const float coef = col > j ? sj * d : 0.f;
+#pragma unroll
+  for (int b = B0; b < kB; ++b) {
+    a[4 * b + 0] = fmaf(-coef, u[b].x, a[4 * b + 0]);
+    a[4 * b + 1] = fmaf(-coef, u[b].y, a[4 * b + 1]);
+    a[4 * b + 2] = fmaf(-coef, u[b].z, a[4 * b + 2]);
+    a[4 * b + 3] = fmaf(-coef, u[b].w, a[4 * b + 3]);
+  }
+  if (pivot) {
+    const int c = j + 1;
+    float tail, alpha;
+    column_stats<NP, B0>(a, c, rg, tail, alpha);
+    tail = col_sum(tail);
+    alpha = col_sum(alpha);
+    if (col == c) {
+      mine = make_reflector(alpha, tail, c == n - 1);
+      publish_u<NP, B0>(sm, a, c, rg, mine.v0);
+      if (rg == 0) sm.S[c] = mine.tau * mine.inv_v0 * mine.inv_v0;
+    }
+  }
+}
+
+// One orgqr step: Q[:, col] -= s_j u_j (u_j^T Q[:, col]).
+template <int NP, int B0>
+__device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[SmallCfg<NP>::kR],
+                                           int j, int rg) {
+  constexpr int kB = SmallCfg<NP>::kB;
+  float4 u[kB];
+#pragma unroll
+  for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
+  const float sj = sm.S[j];
+  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+  for (int b = B0; b < kB; ++b) {
+    d0 = fmaf(u[b].x, q[4 * b + 0], d0);
+    d1 = fmaf(u[b].y, q[4 * b + 1], d1);
+    d2 = fmaf(u[b].z, q[4 * b + 2], d2);
+    d3 = fmaf(u[b].w, q[4 * b + 3], d3);
+  }
+  const float coef = sj * col_sum((d0 + d1) + (d2 + d3));
+#pragma unroll
+  for (int b = B0; b < kB; ++b) {
+    q[4 * b + 0] = fmaf(-coef, u[b].x, q[4 * b + 0]);
+    q[4 * b + 1] = fmaf(-coef, u[b].y, q[4 * b + 1]);
+    q[4 * b + 2] = fmaf(-coef, u[b].z, q[4 * b + 2]);
+    q[4 * b + 3] = fmaf(-coef, u[b].w, q[4 * b + 3]);
+  }
+}
+
+template <int NP>
+__device__ __forceinline__ void geqrf_step_dispatch(SmallSmem<NP>& sm, float (&a)[SmallCfg<NP>::kR],
+                                                    int j, int n, int rg, int col, bool pivot,
+                                                    Reflector& mine) {
+  const int blk = j / SmallCfg<NP>::kBlockRows;
+  if (blk == 0) geqrf_step<NP, 0>(sm, a, j, n, rg, col, pivot, mine);
+  else if (blk == 1) geqrf_step<NP, 1>(sm, a, j, n, rg, col, pivot, mine);
+  else if constexpr (SmallCfg<NP>::kB > 2) {
+    if (blk == 2) geqrf_step<NP, 2>(sm, a, j, n, rg, col, pivot, mine);
+    else geqrf_step<NP, 3>(sm, a, j, n, rg, col, pivot, mine);
+  }
+}
+
+template <int NP>
+__device__ __forceinline__ void orgqr_step_dispatch(const SmallSmem<NP>& sm,
+                                                    float (&q)[SmallCfg<NP>::kR], int j, int rg) {
+  const int blk = j / SmallCfg<NP>::kBlockRows;
+  if (blk == 0) orgqr_step<NP, 0>(sm, q, j, rg);
+  else if (blk == 1) orgqr_step<NP, 1>(sm, q, j, rg);
+  else if constexpr (SmallCfg<NP>::kB > 2) {
+    if (blk == 2) orgqr_step<NP, 2>(sm, q, j, rg);
+    else orgqr_step<NP, 3>(sm, q, j, rg);
+  }
+}
+
+template <int NP>
+__global__ void __launch_bounds__(SmallCfg<NP>::kThreads, 2048 / SmallCfg<NP>::kThreads / 2)
 small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __restrict__ tau,
                 float* __restrict__ Q, int n, int mode) {
   using C = SmallCfg<NP>;
   constexpr int R = C::kR;
-  __shared__ __align__(16) float tile[NP * C::kLD];
-  __shared__ float vbuf[2][NP];
-  __shared__ float taus[NP];
+  __shared__ SmallSmem<NP> sm;
 
-  const int b = blockIdx.x;
+  const int64_t b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rg = lane >> 2, cg = lane & 3;
-  const int col0 = 16 * warp + 4 * cg;       // first of my 4 columns
+  const int rg = lane >> 3, cl = lane & 7;
+  const int col = kCW * warp + cl;
+  const int wlast = kCW * warp + kCW - 1;   // last column of this warp
   const size_t off = (size_t)b * n * n;
+  const bool col_ok = col < n;
 
-  float a[R][4];
+  float a[R];
+  Reflector mine = {0.f, 0.f, 1.f, 1.f};
 
   if (mode & 1) {
-    // ---------------- geqrf ------------------------------------------------
-    load_tile<NP>(tile, A + off, n);
-    __syncthreads();
+    // ---------------- geqrf --------------------------------------------------
 #pragma unroll
     for (int i = 0; i < R; ++i) {
-      float4 v = *reinterpret_cast<const float4*>(tile + (rg + 8 * i) * C::kLD + col0);
-      a[i][0] = v.x; a[i][1] = v.y; a[i][2] = v.z; a[i][3] = v.w;
+      const int row = row_of<NP>(rg, i);
+      a[i] = (row < n && col_ok) ? __ldg(A + off + (size_t)row * n + col) : 0.f;
     }
-
-    for (int j = 0; j < n; ++j) {
-      const int pw = j >> 4, pcg = (j >> 2) & 3, pcc = j & 3;
-      float* vb = vbuf[j & 1];
-      if (warp == pw) {
-        float x[R];
-        float tail = 0.f, alpha = 0.f;
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-          const int r = rg + 8 * i;
-          float xi = pcc == 0 ? a[i][0] : pcc == 1 ? a[i][1] : pcc == 2 ? a[i][2] : a[i][3];
-          x[i] = xi;
-          tail += r > j ? xi * xi : 0.f;
-          alpha += r == j ? xi : 0.f;
-        }
-        tail = rg_sum(tail);
-        alpha = rg_sum(alpha);
-        const Reflector f = make_reflector(alpha, tail, j == n - 1);
-        if (cg == pcg) {
-#pragma unroll
-          for (int i = 0; i < R; ++i) {
-            const int r = rg + 8 * i;
-            const float v = r > j ? x[i] * f.inv_v0 : (r == j ? 1.f : 0.f);
-            vb[r] = v;
-            const float h = r > j ? v : (r == j ? f.beta : x[i]);
-#pragma unroll
-            for (int cc = 0; cc < 4; ++cc)
-              if (cc == pcc) a[i][cc] = h;
-          }
-          if (rg == 0) taus[j] = f.tau;
-        }
-      }
-      __syncthreads();
-      if (16 * warp + 15 > j) {
-        const float t = taus[j];
-        float v[R];
-#pragma unroll
-        for (int i = 0; i < R; ++i) v[i] = vb[rg + 8 * i];
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {
-          float p = 0.f;
-#pragma unroll
-          for (int i = 0; i < R; ++i) p = fmaf(v[i], a[i][cc], p);
-          p = rg_sum(p);
-          const float s = (col0 + cc > j) ? t * p : 0.f;
-#pragma unroll
-          for (int i = 0; i < R; ++i) a[i][cc] = fmaf(-s, v[i], a[i][cc]);
-        }
+    if (warp == 0) {   // reflector of column 0
+      float tail, alpha;
+      column_stats<NP, 0>(a, 0, rg, tail, alpha);
+      tail = col_sum(tail);
+      alpha = col_sum(alpha);
+      if (col == 0) {
+        mine = make_reflector(alpha, tail, n == 1);
+        publish_u<NP, 0>(sm, a, 0, rg, mine.v0);
+        if (rg == 0) sm.S[0] = mine.tau * mine.inv_v0 * mine.inv_v0;
       }
     }
-    // H (registers) -> tile -> global; tau -> global.
+    const int jlast = min(n - 1, wlast);
+    for (int j = 0; j <= jlast; ++j) {
+      named_barrier(1, 32 * (C::kWarps - j / kCW));
+      const bool pivot = (j + 1 < n) && ((j + 1) / kCW == warp);
+      if (wlast > j) geqrf_step_dispatch<NP>(sm, a, j, n, rg, col, pivot, mine);
+    }
+    // H: divide the sub-diagonal of my column by v0, beta on the diagonal.
+    if (col_ok) {
 #pragma unroll
-    for (int i = 0; i < R; ++i)
-      *reinterpret_cast<float4*>(tile + (rg + 8 * i) * C::kLD + col0) =
-          make_float4(a[i][0], a[i][1], a[i][2], a[i][3]);
-    __syncthreads();
-    store_tile<NP>(tile, H + off, n);
-    for (int j = threadIdx.x; j < n; j += C::kThreads) tau[(size_t)b * n + j] = taus[j];
+      for (int i = 0; i < R; ++i) {
+        const int row = row_of<NP>(rg, i);
+        const float h = row > col ? a[i] * mine.inv_v0 : (row == col ? mine.beta : a[i]);
+        if (row < n) H[off + (size_t)row * n + col] = h;
+      }
+      if (rg == 0) tau[(size_t)b * n + col] = mine.tau;
+    }
+    __syncthreads();   // all u_j and s_j published
   } else {
-    load_tile<NP>(tile, H + off, n);
-    for (int j = threadIdx.x; j < n; j += C::kThreads) taus[j] = tau[(size_t)b * n + j];
+    // orgqr only: rebuild u_j = v_j (v0 := 1) and s_j = tau_j from (H, tau).
+    if (col_ok) {
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int row = row_of<NP>(rg, i);
+        a[i] = (row < n && row > col) ? __ldg(H + off + (size_t)row * n + col) : (row == col ? 1.f : 0.f);
+      }
+      if (rg == 0) sm.S[col] = __ldg(tau + (size_t)b * n + col);
+#pragma unroll
+      for (int bb = 0; bb < C::kB; ++bb)
+        sm.U[col][rg][bb] = make_float4(a[4 * bb], a[4 * bb + 1], a[4 * bb + 2], a[4 * bb + 3]);
+    }
     __syncthreads();
   }
 
   if (mode & 2) {
     // ---------------- orgqr: Q = H_0 ... H_{n-1} I, backward ------------------
 #pragma unroll
-    for (int i = 0; i < R; ++i)
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        const int r = rg + 8 * i;
-        a[i][cc] = (r == col0 + cc && r < n) ? 1.f : 0.f;
-      }
+    for (int i = 0; i < R; ++i) a[i] = (row_of<NP>(rg, i) == col && col_ok) ? 1.f : 0.f;
     // Reflector j only touches columns >= j, so a warp starts at its last column.
-    for (int j = min(n - 1, 16 * warp + 15); j >= 0; --j) {
-      const float t = taus[j];
-      float v[R];
+    for (int j = min(n - 1, wlast); j >= 0; --j) orgqr_step_dispatch<NP>(sm, a, j, rg);
+    if (col_ok) {
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        const int r = rg + 8 * i;
-        v[i] = r > j ? tile[r * C::kLD + j] : (r == j ? 1.f : 0.f);
-      }
-#pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        float p = 0.f;
-#pragma unroll
-        for (int i = 0; i < R; ++i) p = fmaf(v[i], a[i][cc], p);
-        p = rg_sum(p) * t;
-#pragma unroll
-        for (int i = 0; i < R; ++i) a[i][cc] = fmaf(-p, v[i], a[i][cc]);
+        const int row = row_of<NP>(rg, i);
+        if (row < n) Q[off + (size_t)row * n + col] = a[i];
       }
     }
-    __syncthreads();   // every warp is done reading reflectors from the tile
-#pragma unroll
-    for (int i = 0; i < R; ++i)
-      *reinterpret_cast<float4*>(tile + (rg + 8 * i) * C::kLD + col0) =
-          make_float4(a[i][0], a[i][1], a[i][2], a[i][3]);
-    __syncthreads();
-    store_tile<NP>(tile, Q + off, n);
   }
 }
 
