@@ -82,6 +82,13 @@ QRB_API int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t ba
 QRB_API int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Returns, and clears, the first error code that a library kernel recorded on the
+ * current device when one of its bounded waits on tensor-core or bulk-copy completion
+ * ran out (0 = none).  Such a kernel skips the rest of its work and exits, so its
+ * output is invalid.  Synchronises with the device.  No counterpart in the reference
+ * (its kernels have no device-side waits). */
+QRB_API int qrb_device_error(void);
+
 /* (H, tau) = geqrf(A) without any caller workspace, for callers that cannot
  * allocate device memory (a plugin host that passes only raw input/output pointers,
  * or a path that must not enter the allocator).  No counterpart in the reference.

@@ -149,6 +149,8 @@ int qrb_last_error(char* buf, size_t len) {
   return g_last_status;
 }
 
+int qrb_device_error(void) { return qrb::take_device_error(); }
+
 size_t qrb_workspace_size(int64_t batch, int n) {
   if (batch < 0 || n < 1 || n > QRB_MAX_N) return 0;
   return ws_bytes(batch, n);

@@ -1,4 +1,6 @@
 // Block reflector application  C[k:, c0:] -= V op(T) (V^T C[k:, c0:])  (SIMT fp32).
+// Used for n % 4 != 0, where TMA cannot describe the rows; other n take the
+// tensor-core kernel in qrb_apply_tc.cu.
 //
 // Replaces the reference's trailing update (_wy_trailing_trisolve,
 // submission.py:434-460: bmm, solve_triangular, baddbmm; and the cublasLt
@@ -178,6 +180,15 @@ apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const fl
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
                          int identity_fill, cudaStream_t s) {
+  if (batch == 0 || c0 >= n) return cudaSuccess;
+  if (apply_tc_supported(n))
+    return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, s);
+  return launch_apply_simt(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, s);
+}
+
+cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, float* C,
+                              int64_t batch, int n, int k, int b, int c0, int trans_t,
+                              int identity_fill, cudaStream_t s) {
   if (batch == 0 || c0 >= n) return cudaSuccess;
   const size_t smem = sizeof(ApplySmem);
   // The opt-in shared-memory limit is a per-device function attribute; set it once per device.

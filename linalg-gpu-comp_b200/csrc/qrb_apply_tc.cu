@@ -1,0 +1,418 @@
+// Block reflector application on the 5th-generation tensor cores:
+//     C[k:, c0:] -= V op(T) (V^T C[k:, c0:])
+// for the trailing update of geqrf (op = T^T) and the backward blocks of orgqr
+// (op = T).  Replaces the reference's cuBLAS bmm / solve_triangular / baddbmm chain
+// (_wy_trailing_trisolve, submission.py:434-460) and its cublasLt BF16x9 trailing
+// GEMMs (submission.py:875-884).
+//
+// One CTA (4 warps) owns one matrix and a 64-column strip of C over all m rows.
+//   phase 1  W^T (64 x 32) = C^T V  : TMA streams 32-row stages of C and V into
+//            shared memory (both operands MN-major, which for tf32 takes the 128-byte
+//            swizzle with 32-byte atoms), threads split every value into three
+//            tf32 pieces (x = x0 + x1 + x2), and one thread issues tcgen05.mma
+//            kind::tf32, M=64 N=32 K=8, for the six products of weight >= 2^-22
+//            (x0y0, x0y1, x1y0, x0y2, x1y1, x2y0), smallest first, one TMEM
+//            accumulator per K step; threads sum the partials in fp32 registers.
+//            Together: fp32 accuracy from the tf32 tensor pipe.
+//   phase 2  W2 = op(T) W in registers (fp32), written K-major/swizzled as 3 pieces.
+//   phase 3  per 128-row tile: TMA loads V and C, tcgen05.mma M=128 N=64 K=32 gives
+//            V W2 in TMEM, the epilogue subtracts it from C in shared memory and a
+//            TMA store writes the tile back.
+// Every mbarrier wait is bounded; a wait that runs out records an error code in
+// g_qrb_device_error and the kernel carries on to its TMEM release and exit.
+// Requires n % 4 == 0 (TMA row strides are multiples of 16 bytes).
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "qrb_internal.cuh"
+#include "qrb_sm100.cuh"
+
+__device__ int g_qrb_device_error = 0;
+__device__ float* g_apply_dbg = nullptr;   // debug: W^T rows and W2 rows of CTA 0
+
+namespace qrb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kTN = 64;        // strip width: phase-1 M, phase-3 N
+constexpr int kR1 = 32;        // rows per phase-1 stage
+constexpr int kR3 = 128;       // rows per phase-3 tile (M)
+constexpr int kThreads = 128;
+// TMEM: phase 1 uses two stage buffers x 4 K-step accumulators x 32 columns, phase 3
+// four K-step accumulators x 64 columns.
+constexpr uint32_t kTmemCols = 256;
+
+// Shared-memory plan (bytes from a 1024-aligned base).  Operands are stored as three
+// tf32 pieces; TMA lands raw fp32 in piece 0, which the split pass overwrites.
+constexpr int kPieces = 3;
+constexpr uint32_t kBox1 = kR1 * 128;            // 32 rows x 32 floats
+constexpr uint32_t kStage1 = 9 * kBox1;          // C pieces 0..2 (2 boxes each), V pieces 0..2
+constexpr uint32_t kBox3 = kR3 * 128;            // 128 rows x 32 floats
+constexpr uint32_t kOffP3C = 0;                  // phase 3 aliases phase 1
+constexpr uint32_t kOffP3V = 2 * kBox3;          // V pieces at kOffP3V + p * kBox3
+constexpr uint32_t kRegionP = 5 * kBox3;         // 80 KB >= 2 * kStage1 (72 KB)
+constexpr uint32_t kWPiece = kTN * 128;          // W2 piece: 64 rows x 32 floats
+constexpr uint32_t kOffW = kRegionP;
+constexpr uint32_t kOffT = kOffW + kPieces * kWPiece;
+constexpr uint32_t kOffBar = kOffT + 32 * 33 * 4 + 32;
+constexpr uint32_t kSmemBytes = kOffBar + 8 * 8 + 16 + 1024;   // + alignment slack
+
+// The six (A piece, B piece) products kept, smallest first.  The tensor core's fp32
+// accumulation rounds each add relative to the running sum, so adding the 2^-22 and
+// 2^-11 terms before the leading one leaves one full-size rounding per K step; each
+// K step also gets its own accumulator and the partials are summed in fp32 registers.
+__device__ __constant__ int kTermA[6] = {2, 1, 0, 1, 0, 0};
+__device__ __constant__ int kTermB[6] = {0, 1, 2, 0, 1, 0};
+
+struct Bars {
+  uint64_t tma1[2], mma1[2], tma3, mma3;
+  uint32_t tmem;
+};
+
+__device__ __forceinline__ void record_error(int code) { atomicCAS(&g_qrb_device_error, 0, code); }
+
+__device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, int code) {
+  if (!mbar_wait(bar, parity)) record_error(code);
+}
+
+// V[r][j] of the unit lower trapezoidal block (r relative to the panel top).
+__device__ __forceinline__ float vmask(float x, int r, int j, int b) {
+  if (j >= b) return 0.f;
+  return r > j ? x : (r == j ? 1.f : 0.f);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_src128,
+                const __grid_constant__ CUtensorMap map_h32, const __grid_constant__ CUtensorMap map_h128,
+                const float* __restrict__ Tg, int n, int k, int b, int c0, int trans_t, int ident,
+                int store_to_h) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  Bars& bars = *reinterpret_cast<Bars*>(sm + kOffBar);
+  float (*Ts)[33] = reinterpret_cast<float (*)[33]>(sm + kOffT);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nstrips = (n - c0 + kTN - 1) / kTN;
+  const int mat = blockIdx.x / nstrips;
+  const int cs = c0 + (int)(blockIdx.x % nstrips) * kTN;
+  const int m = n - k, kb = k + b;
+  const int nst = (m + kR1 - 1) / kR1;
+  const int ntile = (m + kR3 - 1) / kR3;
+
+  if (tid == 0) {
+    mbar_init(&bars.tma1[0], 1);
+    mbar_init(&bars.tma1[1], 1);
+    mbar_init(&bars.mma1[0], 1);
+    mbar_init(&bars.mma1[1], 1);
+    mbar_init(&bars.tma3, 1);
+    mbar_init(&bars.mma3, 1);
+    fence_mbar_init();
+    prefetch_tensormap(&map_src32);
+    prefetch_tensormap(&map_h32);
+  }
+  if (warp == 0) tmem_alloc(&bars.tmem, kTmemCols);
+  // op(T) into shared memory.
+  const float* T = Tg + (size_t)mat * 32 * 32;
+  for (int idx = tid; idx < 32 * 32; idx += kThreads) {
+    const int r = idx >> 5, c = idx & 31;
+    const float t = __ldg(T + idx);
+    if (trans_t) Ts[c][r] = t; else Ts[r][c] = t;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem;
+
+  auto issue_stage = [&](int s) {
+    unsigned char* st = sm + (s & 1) * kStage1;
+    mbar_arrive_expect_tx(&bars.tma1[s & 1], 3 * kBox1);
+    const int y = k + s * kR1;
+    tma_load_3d(st, &map_src32, cs, y, mat, &bars.tma1[s & 1]);
+    tma_load_3d(st + kBox1, &map_src32, cs + 32, y, mat, &bars.tma1[s & 1]);
+    tma_load_3d(st + 6 * kBox1, &map_h32, k, y, mat, &bars.tma1[s & 1]);
+  };
+
+  // ---------------- phase 1: W^T = C^T V ------------------------------------------
+  if (tid == 0) {
+    issue_stage(0);
+    if (nst > 1) issue_stage(1);
+  }
+  constexpr uint32_t idesc1 = idesc_tf32(kTN, 32, 1, 1);
+  const uint32_t tm_lane = (uint32_t)(32 * warp) << 16;   // this warp's TMEM lanes
+  float wacc[32];                                          // W^T row (lanes 0-15 meaningful)
+#pragma unroll
+  for (int j = 0; j < 32; ++j) wacc[j] = 0.f;
+  // Partials of stage s live in TMEM columns (s & 1) * 128 + kk * 32.
+  auto gather_stage = [&](int s) {
+    wait_or_flag(&bars.mma1[s & 1], (s >> 1) & 1, 3);
+    tc_fence_after();
+#pragma unroll 1
+    for (int kk = 0; kk < kR1 / 8; ++kk) {
+      float p[32];
+      tmem_ld32(tmem + tm_lane + (s & 1) * 128 + kk * 32, p);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) wacc[j] += p[j];
+    }
+    tc_fence_before();
+  };
+  for (int s = 0; s < nst; ++s) {
+    const int buf = s & 1;
+    const uint32_t par = (s >> 1) & 1;
+    unsigned char* st = sm + buf * kStage1;
+    wait_or_flag(&bars.tma1[buf], par, 1);
+    // Split C (2 boxes) and V (1 box) into three tf32 pieces, piece 0 in place.
+    for (int e = tid; e < 3 * kR1 * 32; e += kThreads) {
+      const int box = e / (kR1 * 32);               // 0,1: C halves; 2: V
+      const int w = e % (kR1 * 32);
+      const int r = w >> 5, col = w & 31;
+      const uint32_t off = sw128_32b_offset(r, col);
+      unsigned char* p0 = st + (box < 2 ? box * kBox1 : 6 * kBox1);
+      const uint32_t pstride = box < 2 ? 2 * kBox1 : kBox1;
+      float x = *reinterpret_cast<float*>(p0 + off);
+      const int rr = s * kR1 + r;                   // row relative to the panel top
+      if (box == 2) {
+        if (rr < 32) x = vmask(x, rr, col, b);
+        else if (col >= b) x = 0.f;
+      } else if (ident) {
+        const int R = k + rr, Cc = cs + 32 * box + col;
+        if (R < n && Cc < n && (R < kb || Cc < kb)) x = R == Cc ? 1.f : 0.f;
+      }
+      float x0, x1, x2;
+      split3_tf32(x, x0, x1, x2);
+      *reinterpret_cast<float*>(p0 + off) = x0;
+      *reinterpret_cast<float*>(p0 + pstride + off) = x1;
+      *reinterpret_cast<float*>(p0 + 2 * pstride + off) = x2;
+    }
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t base = smem_u32(st);
+#pragma unroll
+      for (int kk = 0; kk < kR1 / 8; ++kk) {   // 8 K rows = 1024 bytes per MMA
+        const uint32_t d = tmem + buf * 128 + kk * 32;
+#pragma unroll
+        for (int t = 0; t < 6; ++t) {
+          const uint64_t ad = sdesc_sw128_32b(base + 2 * kTermA[t] * kBox1 + kk * 1024, kBox1, 512);
+          const uint64_t bd = sdesc_sw128_32b(base + (6 + kTermB[t]) * kBox1 + kk * 1024, kBox1, 512);
+          mma_tf32(d, ad, bd, idesc1, t > 0 ? 1u : 0u);
+        }
+      }
+      mma_commit(&bars.mma1[buf]);
+    }
+    // Fold the previous stage's partials while this stage's MMAs run, then refill.
+    if (s > 0) gather_stage(s - 1);
+    __syncthreads();
+    if (tid == 0 && s + 2 < nst) {
+      // buffer `buf` is read by the MMAs of stage s; wait for them before the refill
+      wait_or_flag(&bars.mma1[buf], par, 2);
+      issue_stage(s + 2);
+    }
+  }
+  gather_stage(nst - 1);
+  tc_fence_after();
+
+  // ---------------- phase 2: W2 = op(T) W  (row i of W^T per lane pair) ---------------
+  {
+    // M = 64 layout: TMEM lanes 0-15 of each warp hold W^T rows 16*warp + lane.
+    float w[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) w[j] = __shfl_sync(0xffffffffu, wacc[j], lane & 15);
+    const int i = 16 * warp + (lane & 15);                 // strip column
+    const int a0 = (lane >> 4) * 16;                       // my 16 outputs
+    if (g_apply_dbg != nullptr && blockIdx.x == 0 && lane < 16)
+      for (int j = 0; j < 32; ++j) g_apply_dbg[i * 32 + j] = w[j];
+    unsigned char* wp = sm + kOffW;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float o[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int a = a0 + 4 * q + e;
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc = fmaf(Ts[a][j], w[j], acc);
+        o[e] = acc;
+      }
+      float x0[4], x1[4], x2[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) split3_tf32(o[e], x0[e], x1[e], x2[e]);
+      const uint32_t off = sw128_offset(i, a0 + 4 * q);
+      *reinterpret_cast<float4*>(wp + off) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+      *reinterpret_cast<float4*>(wp + kWPiece + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+      *reinterpret_cast<float4*>(wp + 2 * kWPiece + off) = make_float4(x2[0], x2[1], x2[2], x2[3]);
+    }
+  }
+  tc_fence_before();
+  fence_proxy_async();
+  __syncthreads();
+  tc_fence_after();
+
+  // ---------------- phase 3: C -= V W2, 128-row tiles -----------------------------------
+  constexpr uint32_t idesc3 = idesc_tf32(kR3, kTN, 0, 0);
+  const CUtensorMap* map_store = store_to_h ? &map_h128 : &map_src128;
+  unsigned char* c3 = sm + kOffP3C;
+  unsigned char* v3 = sm + kOffP3V;
+  for (int t = 0; t < ntile; ++t) {
+    const int y0 = k + t * kR3;
+    if (tid == 0) {
+      if (t > 0) tma_store_wait_read();          // previous tile's store has read c3
+      mbar_arrive_expect_tx(&bars.tma3, 3 * kBox3);
+      tma_load_3d(c3, &map_src128, cs, y0, mat, &bars.tma3);
+      tma_load_3d(c3 + kBox3, &map_src128, cs + 32, y0, mat, &bars.tma3);
+      tma_load_3d(v3, &map_h128, k, y0, mat, &bars.tma3);
+    }
+    wait_or_flag(&bars.tma3, t & 1, 4);
+    for (int e = tid; e < kR3 * 32; e += kThreads) {
+      const int r = e >> 5, col = e & 31;
+      const uint32_t off = sw128_offset(r, col);
+      float x = *reinterpret_cast<float*>(v3 + off);
+      const int rr = t * kR3 + r;
+      if (rr < 32) x = vmask(x, rr, col, b);
+      else if (col >= b) x = 0.f;
+      float x0, x1, x2;
+      split3_tf32(x, x0, x1, x2);
+      *reinterpret_cast<float*>(v3 + off) = x0;
+      *reinterpret_cast<float*>(v3 + kBox3 + off) = x1;
+      *reinterpret_cast<float*>(v3 + 2 * kBox3 + off) = x2;
+    }
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t vb = smem_u32(v3), wb = smem_u32(sm + kOffW);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {   // 8 reflectors = 32 bytes per MMA, own accumulator
+#pragma unroll
+        for (int t3 = 0; t3 < 6; ++t3) {
+          const uint64_t ad = sdesc_sw128(vb + kTermA[t3] * kBox3 + kk * 32, 16, 1024);
+          const uint64_t bd = sdesc_sw128(wb + kTermB[t3] * kWPiece + kk * 32, 16, 1024);
+          mma_tf32(tmem + kk * kTN, ad, bd, idesc3, t3 > 0 ? 1u : 0u);
+        }
+      }
+      mma_commit(&bars.mma3);
+    }
+    wait_or_flag(&bars.mma3, t & 1, 5);
+    tc_fence_after();
+    // Epilogue: row 32*warp + lane of the tile.
+    {
+      const int r = 32 * warp + lane;
+      const int R = y0 + r;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float d[32], p[32];
+        tmem_ld32(tmem + tm_lane + 32 * half, d);
+#pragma unroll 1
+        for (int kk = 1; kk < 4; ++kk) {
+          tmem_ld32(tmem + tm_lane + kk * kTN + 32 * half, p);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) d[j] += p[j];
+        }
+        unsigned char* box = c3 + half * kBox3;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t off = sw128_offset(r, 4 * q);
+          float4 c = *reinterpret_cast<float4*>(box + off);
+          float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int Cc = cs + 32 * half + 4 * q + e;
+            if (ident && R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+            cv[e] -= d[4 * q + e];
+          }
+          *reinterpret_cast<float4*>(box + off) = make_float4(cv[0], cv[1], cv[2], cv[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0) {
+      tma_store_3d(map_store, c3, cs, y0, mat);
+      tma_store_3d(map_store, c3 + kBox3, cs + 32, y0, mat);
+      tma_store_commit();
+    }
+  }
+  if (tid == 0) tma_store_wait_all();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- host: tensor maps -------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* map, const float* base, int64_t batch, int n, int box_rows,
+              CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * n * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool apply_tc_supported(int n) { return n % 4 == 0 && n >= 64 && encode_fn() != nullptr; }
+
+cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C, int64_t batch,
+                            int n, int k, int b, int c0, int trans_t, int identity_fill, cudaStream_t s) {
+  if (batch == 0 || c0 >= n) return cudaSuccess;
+  CUtensorMap m_src32, m_src128, m_h32, m_h128;
+  // Phase-1 boxes feed MN-major operands (32-byte-atom swizzle); phase-3 boxes are
+  // K-major operands and the epilogue tile (plain 128-byte swizzle).
+  const CUtensorMapSwizzle sw1 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, sw3 = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!make_map(&m_src32, src, batch, n, kR1, sw1) || !make_map(&m_src128, src, batch, n, kR3, sw3) ||
+      !make_map(&m_h32, H, batch, n, kR1, sw1) || !make_map(&m_h128, H, batch, n, kR3, sw3))
+    return cudaErrorInvalidValue;
+  static std::atomic<unsigned long long> attr_done{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (!(attr_done.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(apply_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_done.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int store_to_h = (C == H) ? 1 : 0;
+  if (!store_to_h && C != src) return cudaErrorInvalidValue;   // C is either H or the source
+  const unsigned grid = (unsigned)((int64_t)((n - c0 + kTN - 1) / kTN) * batch);
+  apply_tc_kernel<<<grid, kThreads, kSmemBytes, s>>>(m_src32, m_src128, m_h32, m_h128, T, n, k, b, c0,
+                                                      trans_t, identity_fill, store_to_h);
+  return cudaGetLastError();
+}
+
+int take_device_error() {
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_qrb_device_error, sizeof v) != cudaSuccess) return -1;
+  if (v != 0) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_qrb_device_error, &zero, sizeof zero);
+  }
+  return v;
+}
+
+}  // namespace qrb

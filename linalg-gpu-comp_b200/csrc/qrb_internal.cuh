@@ -74,6 +74,19 @@ cudaError_t launch_apply(const float* H, const float* T, const float* src, float
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
                          int identity_fill, cudaStream_t s);
 
+// The two implementations launch_apply dispatches to (SIMT fp32 for any n).
+cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, float* C,
+                              int64_t batch, int n, int k, int b, int c0, int trans_t,
+                              int identity_fill, cudaStream_t s);
+// Tensor-core (tcgen05, 3xTF32) variant of launch_apply; needs n % 4 == 0.
+bool apply_tc_supported(int n);
+cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C,
+                            int64_t batch, int n, int k, int b, int c0, int trans_t,
+                            int identity_fill, cudaStream_t s);
+
+// First error code recorded by a kernel whose bounded wait ran out (0 = none); clears it.
+int take_device_error();
+
 // T factors of all panels from (H, tau), for orgqr without a preceding geqrf.
 cudaError_t launch_larft(const float* H, const float* tau, float* T_all,
                          int64_t batch, int n, cudaStream_t s);

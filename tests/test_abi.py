@@ -27,7 +27,7 @@ def declared_symbols():
 def test_header_declares_the_api():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
-        "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc"}
+        "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error"}
 
 
 def test_library_exports_every_declared_symbol(lib):

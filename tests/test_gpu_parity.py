@@ -246,3 +246,9 @@ def test_workspace_too_small_is_reported():
     st = _lib.lib().qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), t.data_ptr(), 2, 100, None, 0,
                                   torch.cuda.current_stream().cuda_stream)
     assert st == _lib.QRB_ERR_WORKSPACE
+
+
+def test_no_kernel_recorded_a_wait_timeout():
+    """Every bounded device-side wait of the kernels above completed."""
+    from qr_b200 import _lib
+    assert _lib.lib().qrb_device_error() == 0
