@@ -30,7 +30,6 @@
 #include "qrb_sm100.cuh"
 
 __device__ int g_qrb_device_error = 0;
-__device__ float* g_apply_dbg = nullptr;   // debug: W^T rows and W2 rows of CTA 0
 
 namespace qrb {
 namespace {
@@ -224,8 +223,6 @@ apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_cons
     for (int j = 0; j < 32; ++j) w[j] = __shfl_sync(0xffffffffu, wacc[j], lane & 15);
     const int i = 16 * warp + (lane & 15);                 // strip column
     const int a0 = (lane >> 4) * 16;                       // my 16 outputs
-    if (g_apply_dbg != nullptr && blockIdx.x == 0 && lane < 16)
-      for (int j = 0; j < 32; ++j) g_apply_dbg[i * 32 + j] = w[j];
     unsigned char* wp = sm + kOffW;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
