@@ -16,9 +16,9 @@
 //      values in the same order, so all agree bit-for-bit on beta and tau;
 //   3. each lane forms its partial w_c = v^T a_c; reduced the same way;
 //   4. lanes c > j apply a_c -= tau w_c v; lane j stores beta / v.
-// For c < j the reduced w_c equals (V^T V)[c, j], so the T recurrence
-// T[:j, j] = -tau_j T[:j, :j] G[:j, j] (submissions/v1.py:48-56) is evaluated by
-// warp 0 in the same pass, with no separate Gram product.
+// For c < j the reduced w_c equals (V^T V)[c, j], so the Gram matrix of the T
+// recurrence T[:j, j] = -tau_j T[:j, :j] G[:j, j] (submissions/v1.py:48-56) falls out
+// of the same pass; warp 0 evaluates the recurrence row-parallel after the loop.
 #include <cooperative_groups.h>
 
 #include "qrb_internal.cuh"
@@ -40,6 +40,8 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   __shared__ float red_w[2][kPanelWarps][32];     // per-warp w partials
   __shared__ float red_c[2][CL][32];              // per-CTA w partials (CL > 1)
   __shared__ float Ts[32][33];                    // T factor (rank 0 only)
+  __shared__ float Gs[32][33];                    // strict upper part of V^T V (rank 0)
+  __shared__ float taus[32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int rank = 0;
@@ -138,13 +140,39 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
         a[i] = pr > j ? v[i] : (pr == j ? f.beta : a[i]);
       }
     }
-    // ---- T column j (warp 0 of rank 0); lane c < j holds G[c][j] in w ---------
+    // ---- record G[:j, j] (lane c < j holds it in w) and tau_j (warp 0 of rank 0) --
     if (warp == 0 && rank == 0) {
-      float t = 0.f;
-      for (int c = 0; c < j; ++c) t = fmaf(Ts[lane][c], __shfl_sync(0xffffffffu, w, c), t);
-      if (lane < j) Ts[lane][j] = -f.tau * t;
-      else if (lane == j) Ts[lane][j] = f.tau;
-      if (lane == 0) tau[(size_t)mat * n + k + j] = f.tau;
+      if (lane < j) Gs[lane][j] = w;
+      if (lane == 0) {
+        taus[j] = f.tau;
+        tau[(size_t)mat * n + k + j] = f.tau;
+      }
+    }
+  }
+
+  // ---- T factor after the column loop: lane i builds row i of T ------------------
+  // T[i][j] = -tau_j * sum_{c=i}^{j-1} T[i][c] G[c][j] (j > i), T[i][i] = tau_i: rows are
+  // independent, so the 32 recurrences run side by side instead of one per column step.
+  if (warp == 0 && rank == 0) {
+    __syncwarp();
+    const int i = lane;
+    for (int j = 0; j < 32; ++j) {
+      float t;
+      if (j < i || j >= b) {
+        t = 0.f;
+      } else if (j == i) {
+        t = taus[j];
+      } else {
+        float s0 = 0.f, s1 = 0.f;
+        int c = i;
+        for (; c + 1 < j; c += 2) {
+          s0 = fmaf(Ts[i][c], Gs[c][j], s0);
+          s1 = fmaf(Ts[i][c + 1], Gs[c + 1][j], s1);
+        }
+        if (c < j) s0 = fmaf(Ts[i][c], Gs[c][j], s0);
+        t = -taus[j] * (s0 + s1);
+      }
+      Ts[i][j] = t;
     }
   }
 
@@ -155,6 +183,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     if (pr < m && lane < b) H[moff + (size_t)(k + pr) * n + k + lane] = a[i];
   }
   if (warp == 0 && rank == 0) {
+    __syncwarp();
     float* T = Tout + (size_t)mat * 32 * 32;
 #pragma unroll 4
     for (int r = 0; r < 32; ++r) T[r * 32 + lane] = Ts[r][lane];
