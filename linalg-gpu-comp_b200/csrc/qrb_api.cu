@@ -8,7 +8,8 @@
 //                trailing update A[k:, k+32:] -= V T^T V^T A (qrb_apply.cu);
 //              Q by backward block accumulation Q[k:, k:] -= V T V^T Q[k:, k:]
 //              over the same T factors, with the identity generated on the fly.
-// Workspace: the T factors of every panel, [panel][batch][32][32] fp32.
+// Workspace: the T factors of every panel, [panel][batch][32][32] fp32, then the
+// tf32 pieces of one panel's V for the tensor-core update (see ws_bytes).
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -39,9 +40,22 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 int n_panels(int n) { return (n + qrb::kNB - 1) / qrb::kNB; }
 
+size_t t_bytes(int64_t batch, int n) {
+  return (size_t)n_panels(n) * (size_t)batch * qrb::kNB * qrb::kNB * sizeof(float);
+}
+
+// Workspace: the T factors of every panel, then (for the tensor-core path, n % 4 == 0)
+// one panel's V split into three tf32 pieces, [piece][batch][n][32] fp32.
 size_t ws_bytes(int64_t batch, int n) {
   if (n <= qrb::kSmallMaxN) return 0;
-  return (size_t)n_panels(n) * (size_t)batch * qrb::kNB * qrb::kNB * sizeof(float);
+  size_t bytes = t_bytes(batch, n);
+  if (n % 4 == 0) bytes = ((bytes + 255) & ~size_t(255)) + qrb::vprep_floats(batch, n) * sizeof(float);
+  return bytes;
+}
+
+float* vprep_ws(void* ws, int64_t batch, int n) {
+  if (n % 4 != 0) return nullptr;
+  return reinterpret_cast<float*>(static_cast<char*>(ws) + ((t_bytes(batch, n) + 255) & ~size_t(255)));
 }
 
 // The kernels are built for sm_100a only: refuse anything else up front rather
@@ -109,7 +123,7 @@ int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, vo
     float* T = panel_T(ws, batch, p);
     QRB_CUDA(qrb::launch_panel(src, H, tau, T, batch, n, k, b, s), "panel kernel launch");
     if (k + b < n)
-      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, s), "trailing update launch");
+      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, vprep_ws(ws, batch, n), s), "trailing update launch");
   }
   return QRB_OK;
 }
@@ -117,7 +131,7 @@ int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, vo
 int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
   for (int p = n_panels(n) - 1; p >= 0; --p) {
     const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
-    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, s),
+    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, vprep_ws(ws, batch, n), s),
              "orgqr block launch");
   }
   return QRB_OK;

@@ -93,7 +93,7 @@ extern "C" QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* ta
     const float* src = k == 0 ? A : H;
     if (qrb::launch_panel(src, H, tau, T, batch, n, k, b, s) != cudaSuccess) return QRB_ERR_CUDA;
     if (k + b < n &&
-        qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, s) != cudaSuccess)
+        qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, nullptr, s) != cudaSuccess)
       return QRB_ERR_CUDA;
   }
   return QRB_OK;
