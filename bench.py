@@ -58,7 +58,9 @@ def kernel_launches(n: int) -> int:
     if n <= 64:
         return 1
     np_ = (n + 31) // 32
-    return np_ + (np_ - 1) + np_      # panels + trailing updates + orgqr blocks
+    applies = (np_ - 1) + np_         # trailing updates + orgqr blocks
+    vsplits = applies if n % 4 == 0 else 0   # tensor-core path: one V split per update
+    return np_ + applies + vsplits
 
 
 def dominant_kernel(n: int) -> str:
