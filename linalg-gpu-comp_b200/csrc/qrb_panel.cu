@@ -62,18 +62,33 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     for (int c = 0; c < 32; ++c) Ts[lane][c] = 0.f;
   }
 
+  // Reflectors are applied unscaled: u_j = (0.., v0, x_{j+1}, ..) and H_j = I - s u u^T
+  // with s = tau / v0^2, so no lane rescales its rows per step; lane c keeps its raw
+  // column and divides it by v0_c once at the end.  Only registers i < kTop can hold
+  // a row <= 31 (rank 0); every other row is below any pivot of the panel and needs no
+  // row predicate.
+  constexpr int kTop = 4;
+  float my_inv = 1.f, my_beta = 0.f;   // this lane's column reflector (set at step j == lane)
   for (int j = 0; j < b; ++j) {
     const int par = j & 1;
     // ---- 1. column j of my rows, partial norms --------------------------------
-    float v[RPT];   // column j of my rows; turned into the reflector in step 3
-    float tail = 0.f, alpha = 0.f;
+    float u[RPT];
+    float tail = 0.f, tail2 = 0.f, alpha = 0.f;
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const int pr = row0 + 8 * i;
-      v[i] = __shfl_sync(0xffffffffu, a[i], j);
-      tail += pr > j ? v[i] * v[i] : 0.f;
-      alpha += pr == j ? v[i] : 0.f;
+      const float x = __shfl_sync(0xffffffffu, a[i], j);
+      u[i] = x;
+      if (i < kTop) {
+        tail += pr > j ? x * x : 0.f;
+        alpha += pr == j ? x : 0.f;
+      } else if (i & 1) {
+        tail2 = fmaf(x, x, tail2);
+      } else {
+        tail = fmaf(x, x, tail);
+      }
     }
+    tail += tail2;
     // ---- 2. combine (tail^2, alpha) -------------------------------------------
     if constexpr (CL == 1) {
       if (lane == 0) red_n[par][warp] = make_float2(tail, alpha);
@@ -100,15 +115,15 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     }
     const Reflector f = make_reflector(alpha, tail, j == m - 1);
 
-    // ---- 3. w_c = v^T a_c ------------------------------------------------------
-    float wp = 0.f;
+    // ---- 3. w_c = u^T a_c (= v0 * v^T a_c) --------------------------------------
+    float wp = 0.f, wp2 = 0.f;
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const int pr = row0 + 8 * i;
-      v[i] = pr > j ? v[i] * f.inv_v0 : (pr == j ? 1.f : 0.f);
-      wp = fmaf(v[i], a[i], wp);
+      if (i < kTop) u[i] = pr > j ? u[i] : (pr == j ? f.v0 : 0.f);
+      if (i & 1) wp2 = fmaf(u[i], a[i], wp2); else wp = fmaf(u[i], a[i], wp);
     }
-    red_w[par][warp][lane] = wp;
+    red_w[par][warp][lane] = wp + wp2;
     __syncthreads();
     float w = 0.f;
     if constexpr (CL == 1) {
@@ -128,21 +143,18 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
       for (int q = 0; q < CL; ++q) w += red_c[par][q][lane];
     }
 
-    // ---- 4. apply to columns > j, store column j -------------------------------
-    if (lane > j) {
-      const float s = f.tau * w;
+    // ---- 4. apply to columns > j (lane j keeps its raw column) -------------------
+    const float coef = lane > j ? f.tau * f.inv_v0 * f.inv_v0 * w : 0.f;
 #pragma unroll
-      for (int i = 0; i < RPT; ++i) a[i] = fmaf(-s, v[i], a[i]);
-    } else if (lane == j) {
-#pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        const int pr = row0 + 8 * i;
-        a[i] = pr > j ? v[i] : (pr == j ? f.beta : a[i]);
-      }
+    for (int i = 0; i < RPT; ++i) a[i] = fmaf(-coef, u[i], a[i]);
+    if (lane == j) {
+      my_inv = f.inv_v0;
+      my_beta = f.beta;
     }
-    // ---- record G[:j, j] (lane c < j holds it in w) and tau_j (warp 0 of rank 0) --
+    // ---- record G[:j, j] = (V^T V)[c, j] and tau_j (warp 0 of rank 0) ----------
+    // Lane c < j holds raw column c, so w = v0_j v0_c G[c][j].
     if (warp == 0 && rank == 0) {
-      if (lane < j) Gs[lane][j] = w;
+      if (lane < j) Gs[lane][j] = w * f.inv_v0 * my_inv;
       if (lane == 0) {
         taus[j] = f.tau;
         tau[(size_t)mat * n + k + j] = f.tau;
@@ -176,11 +188,13 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     }
   }
 
-  // ---- write back panel and T ---------------------------------------------------
+  // ---- write back panel (v = raw / v0 below, beta on the diagonal) and T ------
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
     const int pr = row0 + 8 * i;
-    if (pr < m && lane < b) H[moff + (size_t)(k + pr) * n + k + lane] = a[i];
+    float h = a[i] * my_inv;
+    if (i < kTop) h = pr > lane ? h : (pr == lane ? my_beta : a[i]);
+    if (pr < m && lane < b) H[moff + (size_t)(k + pr) * n + k + lane] = h;
   }
   if (warp == 0 && rank == 0) {
     __syncwarp();
