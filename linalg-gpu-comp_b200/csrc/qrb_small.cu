@@ -7,8 +7,9 @@
 // (reference_repo/reference.py:144).
 //
 // Layout.  NP (32 or 64) is n rounded up.  Four lanes share a column: lane =
-// 8*rg + cl (rg in 0..3) of warp w owns column 8w + cl and the rows {rg + 4i}, all
-// in registers, so the CTA has NP/8 warps.  A column reduction over rows is a
+// 8*rg + cl (rg in 0..3) of warp w owns columns 16w + cl and 16w + 8 + cl and the
+// rows {rg + 4i}, all in registers, so the CTA has NP/16 warps (small register
+// footprint per matrix: more matrices in flight per SM).  A column reduction over rows is a
 // register sum plus two xor shuffles (8, 16).
 //
 // Reflectors are published unscaled: u_j = (0.., v0, x_{j+1}, .., x_{n-1}) with
@@ -29,7 +30,8 @@ namespace qrb {
 namespace {
 
 constexpr int kRG = 4;            // lanes per column
-constexpr int kCW = 32 / kRG;     // columns per warp
+constexpr int kCPL = 2;           // columns per lane
+constexpr int kCW = 32 / kRG * kCPL;   // columns per warp
 
 template <int NP>
 struct SmallCfg {
@@ -104,90 +106,112 @@ __device__ __forceinline__ void column_stats(const float (&a)[SmallCfg<NP>::kR],
   tail = t0 + t1;
 }
 
-// One geqrf step: apply H_j (u_j, s_j) to this lane's column; if `pivot`, also
-// produce the reflector of column j+1 (owned by lanes with col == j+1).
+// One geqrf step: apply H_j (u_j, s_j) to this lane's columns; if `pivot`, also
+// produce the reflector of column j+1 (held in a[pk] by lanes with cl == (j+1) % 8).
 template <int NP, int B0>
-__device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[SmallCfg<NP>::kR], int j,
-                                           int n, int rg, int col, bool pivot, Reflector& mine) {
+__device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][SmallCfg<NP>::kR], int j,
+                                           int n, int rg, int col0, bool pivot, Reflector (&mine)[kCPL]) {
   constexpr int kB = SmallCfg<NP>::kB;
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
-  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+  float d[kCPL];
 #pragma unroll
-  for (int b = B0; b < kB; ++b) {
-    d0 = fmaf(u[b].x, a[4 * b + 0], d0);
-    d1 = fmaf(u[b].y, a[4 * b + 1], d1);
-    d2 = fmaf(u[b].z, a[4 * b + 2], d2);
-    d3 = fmaf(u[b].w, a[4 * b + 3], d3);
+  for (int kk = 0; kk < kCPL; ++kk) {
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+    for (int b = B0; b < kB; ++b) {
+      d0 = fmaf(u[b].x, a[kk][4 * b + 0], d0);
+      d1 = fmaf(u[b].y, a[kk][4 * b + 1], d1);
+      d2 = fmaf(u[b].z, a[kk][4 * b + 2], d2);
+      d3 = fmaf(u[b].w, a[kk][4 * b + 3], d3);
+    }
+    d[kk] = (d0 + d1) + (d2 + d3);
   }
-  const float d = col_sum((d0 + d1) + (d2 + d3));
-  const float coef = col > j ? sj * d : 0.f;
 #pragma unroll
-  for (int b = B0; b < kB; ++b) {
-    a[4 * b + 0] = fmaf(-coef, u[b].x, a[4 * b + 0]);
-    a[4 * b + 1] = fmaf(-coef, u[b].y, a[4 * b + 1]);
-    a[4 * b + 2] = fmaf(-coef, u[b].z, a[4 * b + 2]);
-    a[4 * b + 3] = fmaf(-coef, u[b].w, a[4 * b + 3]);
+  for (int kk = 0; kk < kCPL; ++kk) d[kk] = col_sum(d[kk]);
+#pragma unroll
+  for (int kk = 0; kk < kCPL; ++kk) {
+    const float coef = col0 + 8 * kk > j ? sj * d[kk] : 0.f;
+#pragma unroll
+    for (int b = B0; b < kB; ++b) {
+      a[kk][4 * b + 0] = fmaf(-coef, u[b].x, a[kk][4 * b + 0]);
+      a[kk][4 * b + 1] = fmaf(-coef, u[b].y, a[kk][4 * b + 1]);
+      a[kk][4 * b + 2] = fmaf(-coef, u[b].z, a[kk][4 * b + 2]);
+      a[kk][4 * b + 3] = fmaf(-coef, u[b].w, a[kk][4 * b + 3]);
+    }
   }
   if (pivot) {
     const int c = j + 1;
-    float tail, alpha;
-    column_stats<NP, B0>(a, c, rg, tail, alpha);
-    tail = col_sum(tail);
-    alpha = col_sum(alpha);
-    if (col == c) {
-      mine = make_reflector(alpha, tail, c == n - 1);
-      publish_u<NP, B0>(sm, a, c, rg, mine.v0);
-      if (rg == 0) sm.S[c] = mine.tau * mine.inv_v0 * mine.inv_v0;
+    const int pk = (c % kCW) >> 3;
+#pragma unroll
+    for (int kk = 0; kk < kCPL; ++kk) {
+      if (kk != pk) continue;
+      float tail, alpha;
+      column_stats<NP, B0>(a[kk], c, rg, tail, alpha);
+      tail = col_sum(tail);
+      alpha = col_sum(alpha);
+      if (col0 + 8 * kk == c) {
+        mine[kk] = make_reflector(alpha, tail, c == n - 1);
+        publish_u<NP, B0>(sm, a[kk], c, rg, mine[kk].v0);
+        if (rg == 0) sm.S[c] = mine[kk].tau * mine[kk].inv_v0 * mine[kk].inv_v0;
+      }
     }
   }
 }
 
-// One orgqr step: Q[:, col] -= s_j u_j (u_j^T Q[:, col]).
+// One orgqr step: Q[:, col] -= s_j u_j (u_j^T Q[:, col]) for this lane's columns.
 template <int NP, int B0>
-__device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[SmallCfg<NP>::kR],
+__device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[kCPL][SmallCfg<NP>::kR],
                                            int j, int rg) {
   constexpr int kB = SmallCfg<NP>::kB;
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
-  float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+  float d[kCPL];
 #pragma unroll
-  for (int b = B0; b < kB; ++b) {
-    d0 = fmaf(u[b].x, q[4 * b + 0], d0);
-    d1 = fmaf(u[b].y, q[4 * b + 1], d1);
-    d2 = fmaf(u[b].z, q[4 * b + 2], d2);
-    d3 = fmaf(u[b].w, q[4 * b + 3], d3);
+  for (int kk = 0; kk < kCPL; ++kk) {
+    float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
+#pragma unroll
+    for (int b = B0; b < kB; ++b) {
+      d0 = fmaf(u[b].x, q[kk][4 * b + 0], d0);
+      d1 = fmaf(u[b].y, q[kk][4 * b + 1], d1);
+      d2 = fmaf(u[b].z, q[kk][4 * b + 2], d2);
+      d3 = fmaf(u[b].w, q[kk][4 * b + 3], d3);
+    }
+    d[kk] = (d0 + d1) + (d2 + d3);
   }
-  const float coef = sj * col_sum((d0 + d1) + (d2 + d3));
 #pragma unroll
-  for (int b = B0; b < kB; ++b) {
-    q[4 * b + 0] = fmaf(-coef, u[b].x, q[4 * b + 0]);
-    q[4 * b + 1] = fmaf(-coef, u[b].y, q[4 * b + 1]);
-    q[4 * b + 2] = fmaf(-coef, u[b].z, q[4 * b + 2]);
-    q[4 * b + 3] = fmaf(-coef, u[b].w, q[4 * b + 3]);
+  for (int kk = 0; kk < kCPL; ++kk) {
+    const float coef = sj * col_sum(d[kk]);
+#pragma unroll
+    for (int b = B0; b < kB; ++b) {
+      q[kk][4 * b + 0] = fmaf(-coef, u[b].x, q[kk][4 * b + 0]);
+      q[kk][4 * b + 1] = fmaf(-coef, u[b].y, q[kk][4 * b + 1]);
+      q[kk][4 * b + 2] = fmaf(-coef, u[b].z, q[kk][4 * b + 2]);
+      q[kk][4 * b + 3] = fmaf(-coef, u[b].w, q[kk][4 * b + 3]);
+    }
   }
 }
 
 template <int NP>
-__device__ __forceinline__ void geqrf_step_dispatch(SmallSmem<NP>& sm, float (&a)[SmallCfg<NP>::kR],
-                                                    int j, int n, int rg, int col, bool pivot,
-                                                    Reflector& mine) {
+__device__ __forceinline__ void geqrf_step_dispatch(SmallSmem<NP>& sm, float (&a)[kCPL][SmallCfg<NP>::kR],
+                                                    int j, int n, int rg, int col0, bool pivot,
+                                                    Reflector (&mine)[kCPL]) {
   const int blk = j / SmallCfg<NP>::kBlockRows;
-  if (blk == 0) geqrf_step<NP, 0>(sm, a, j, n, rg, col, pivot, mine);
-  else if (blk == 1) geqrf_step<NP, 1>(sm, a, j, n, rg, col, pivot, mine);
+  if (blk == 0) geqrf_step<NP, 0>(sm, a, j, n, rg, col0, pivot, mine);
+  else if (blk == 1) geqrf_step<NP, 1>(sm, a, j, n, rg, col0, pivot, mine);
   else if constexpr (SmallCfg<NP>::kB > 2) {
-    if (blk == 2) geqrf_step<NP, 2>(sm, a, j, n, rg, col, pivot, mine);
-    else geqrf_step<NP, 3>(sm, a, j, n, rg, col, pivot, mine);
+    if (blk == 2) geqrf_step<NP, 2>(sm, a, j, n, rg, col0, pivot, mine);
+    else geqrf_step<NP, 3>(sm, a, j, n, rg, col0, pivot, mine);
   }
 }
 
 template <int NP>
 __device__ __forceinline__ void orgqr_step_dispatch(const SmallSmem<NP>& sm,
-                                                    float (&q)[SmallCfg<NP>::kR], int j, int rg) {
+                                                    float (&q)[kCPL][SmallCfg<NP>::kR], int j, int rg) {
   const int blk = j / SmallCfg<NP>::kBlockRows;
   if (blk == 0) orgqr_step<NP, 0>(sm, q, j, rg);
   else if (blk == 1) orgqr_step<NP, 1>(sm, q, j, rg);
@@ -198,7 +222,7 @@ __device__ __forceinline__ void orgqr_step_dispatch(const SmallSmem<NP>& sm,
 }
 
 template <int NP>
-__global__ void __launch_bounds__(SmallCfg<NP>::kThreads, 2048 / SmallCfg<NP>::kThreads / 2)
+__global__ void __launch_bounds__(SmallCfg<NP>::kThreads, NP == 64 ? 7 : 8)
 small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __restrict__ tau,
                 float* __restrict__ Q, int n, int mode) {
   using C = SmallCfg<NP>;
@@ -208,61 +232,72 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
   const int64_t b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = lane >> 3, cl = lane & 7;
-  const int col = kCW * warp + cl;
+  const int col0 = kCW * warp + cl;         // my columns: col0 + 8 * kk
   const int wlast = kCW * warp + kCW - 1;   // last column of this warp
   const size_t off = (size_t)b * n * n;
-  const bool col_ok = col < n;
 
-  float a[R];
-  Reflector mine = {0.f, 0.f, 1.f, 1.f};
+  float a[kCPL][R];
+  Reflector mine[kCPL];
+#pragma unroll
+  for (int kk = 0; kk < kCPL; ++kk) mine[kk] = {0.f, 0.f, 1.f, 1.f};
 
   if (mode & 1) {
     // ---------------- geqrf --------------------------------------------------
 #pragma unroll
-    for (int i = 0; i < R; ++i) {
-      const int row = row_of<NP>(rg, i);
-      a[i] = (row < n && col_ok) ? __ldg(A + off + (size_t)row * n + col) : 0.f;
-    }
+    for (int kk = 0; kk < kCPL; ++kk)
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        const int row = row_of<NP>(rg, i), col = col0 + 8 * kk;
+        a[kk][i] = (row < n && col < n) ? __ldg(A + off + (size_t)row * n + col) : 0.f;
+      }
     if (warp == 0) {   // reflector of column 0
       float tail, alpha;
-      column_stats<NP, 0>(a, 0, rg, tail, alpha);
+      column_stats<NP, 0>(a[0], 0, rg, tail, alpha);
       tail = col_sum(tail);
       alpha = col_sum(alpha);
-      if (col == 0) {
-        mine = make_reflector(alpha, tail, n == 1);
-        publish_u<NP, 0>(sm, a, 0, rg, mine.v0);
-        if (rg == 0) sm.S[0] = mine.tau * mine.inv_v0 * mine.inv_v0;
+      if (col0 == 0) {
+        mine[0] = make_reflector(alpha, tail, n == 1);
+        publish_u<NP, 0>(sm, a[0], 0, rg, mine[0].v0);
+        if (rg == 0) sm.S[0] = mine[0].tau * mine[0].inv_v0 * mine[0].inv_v0;
       }
     }
     const int jlast = min(n - 1, wlast);
     for (int j = 0; j <= jlast; ++j) {
       named_barrier(1, 32 * (C::kWarps - j / kCW));
       const bool pivot = (j + 1 < n) && ((j + 1) / kCW == warp);
-      if (wlast > j) geqrf_step_dispatch<NP>(sm, a, j, n, rg, col, pivot, mine);
+      if (wlast > j) geqrf_step_dispatch<NP>(sm, a, j, n, rg, col0, pivot, mine);
     }
-    // H: divide the sub-diagonal of my column by v0, beta on the diagonal.
-    if (col_ok) {
+    // H: divide the sub-diagonal of each column by its v0, beta on the diagonal.
 #pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const int row = row_of<NP>(rg, i);
-        const float h = row > col ? a[i] * mine.inv_v0 : (row == col ? mine.beta : a[i]);
-        if (row < n) H[off + (size_t)row * n + col] = h;
+    for (int kk = 0; kk < kCPL; ++kk) {
+      const int col = col0 + 8 * kk;
+      if (col < n) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const int row = row_of<NP>(rg, i);
+          const float h = row > col ? a[kk][i] * mine[kk].inv_v0 : (row == col ? mine[kk].beta : a[kk][i]);
+          if (row < n) H[off + (size_t)row * n + col] = h;
+        }
+        if (rg == 0) tau[(size_t)b * n + col] = mine[kk].tau;
       }
-      if (rg == 0) tau[(size_t)b * n + col] = mine.tau;
     }
     __syncthreads();   // all u_j and s_j published
   } else {
     // orgqr only: rebuild u_j = v_j (v0 := 1) and s_j = tau_j from (H, tau).
-    if (col_ok) {
 #pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const int row = row_of<NP>(rg, i);
-        a[i] = (row < n && row > col) ? __ldg(H + off + (size_t)row * n + col) : (row == col ? 1.f : 0.f);
+    for (int kk = 0; kk < kCPL; ++kk) {
+      const int col = col0 + 8 * kk;
+      if (col < n) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const int row = row_of<NP>(rg, i);
+          a[kk][i] = (row < n && row > col) ? __ldg(H + off + (size_t)row * n + col) : (row == col ? 1.f : 0.f);
+        }
+        if (rg == 0) sm.S[col] = __ldg(tau + (size_t)b * n + col);
+#pragma unroll
+        for (int bb = 0; bb < C::kB; ++bb)
+          sm.U[col][rg][bb] = make_float4(a[kk][4 * bb], a[kk][4 * bb + 1], a[kk][4 * bb + 2], a[kk][4 * bb + 3]);
       }
-      if (rg == 0) sm.S[col] = __ldg(tau + (size_t)b * n + col);
-#pragma unroll
-      for (int bb = 0; bb < C::kB; ++bb)
-        sm.U[col][rg][bb] = make_float4(a[4 * bb], a[4 * bb + 1], a[4 * bb + 2], a[4 * bb + 3]);
     }
     __syncthreads();
   }
@@ -270,14 +305,21 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
   if (mode & 2) {
     // ---------------- orgqr: Q = H_0 ... H_{n-1} I, backward ------------------
 #pragma unroll
-    for (int i = 0; i < R; ++i) a[i] = (row_of<NP>(rg, i) == col && col_ok) ? 1.f : 0.f;
+    for (int kk = 0; kk < kCPL; ++kk)
+#pragma unroll
+      for (int i = 0; i < R; ++i)
+        a[kk][i] = (row_of<NP>(rg, i) == col0 + 8 * kk && col0 + 8 * kk < n) ? 1.f : 0.f;
     // Reflector j only touches columns >= j, so a warp starts at its last column.
     for (int j = min(n - 1, wlast); j >= 0; --j) orgqr_step_dispatch<NP>(sm, a, j, rg);
-    if (col_ok) {
 #pragma unroll
-      for (int i = 0; i < R; ++i) {
-        const int row = row_of<NP>(rg, i);
-        if (row < n) Q[off + (size_t)row * n + col] = a[i];
+    for (int kk = 0; kk < kCPL; ++kk) {
+      const int col = col0 + 8 * kk;
+      if (col < n) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+          const int row = row_of<NP>(rg, i);
+          if (row < n) Q[off + (size_t)row * n + col] = a[kk][i];
+        }
       }
     }
   }
