@@ -46,9 +46,9 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bo
   float v0 = alpha - beta;
   float vn2 = v0 * v0 + tail2;
   r.beta = beta;
-  r.tau = vn2 > 0.f ? (2.f * v0 * v0) / vn2 : 0.f;
+  r.tau = vn2 > 0.f ? __fdividef(2.f * v0 * v0, vn2) : 0.f;   // short-latency division on the serial path
   r.v0 = fabsf(v0) < kEpsV0 ? 1.f : v0;
-  r.inv_v0 = 1.f / r.v0;
+  r.inv_v0 = __fdividef(1.f, r.v0);
   return r;
 }
 
