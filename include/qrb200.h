@@ -100,6 +100,24 @@ QRB_API int qrb_device_error(void);
 QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch, int n,
                                   void* stream);
 
+/* Device workspace, in bytes, of qrb_qr_f32_host for this batch (with_q != 0: Q is
+ * formed too); 0 for invalid sizes or an empty batch. */
+QRB_API size_t qrb_host_workspace_size(int64_t batch, int n, int with_q);
+
+/* The same QR with HOST buffers: A (batch x n x n) is read from host memory and H,
+ * tau and, when Q is not NULL, Q are written to host memory.  The batch is cut into
+ * chunks whose copy-in, factorisation and copy-out overlap on internal streams;
+ * `stream` orders the whole call (it waits for the caller's earlier work on it and
+ * the caller's later work on it waits for the last copy).  Host buffers should be
+ * page-locked (cudaHostAlloc / cudaHostRegister) for the copies to overlap; A may
+ * alias H.  `device_workspace` is device memory of qrb_host_workspace_size bytes,
+ * 256-byte aligned.  Results are identical to qrb_qr_f32 / qrb_geqrf_f32.  No
+ * counterpart in the reference, whose harness keeps inputs and outputs on the device
+ * (reference_repo/eval.py:128-131); this serves callers whose batch lives in host
+ * memory. */
+QRB_API int qrb_qr_f32_host(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
+                            void* device_workspace, size_t device_workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -13,6 +13,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/qrb200.h"
@@ -137,6 +138,141 @@ int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cuda
   return QRB_OK;
 }
 
+// (H, tau[, Q]) of a device batch on stream s; arguments already checked.
+int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  if (n <= qrb::kSmallMaxN) {
+    QRB_CUDA(qrb::launch_small(A, H, tau, Q, batch, n, Q != nullptr ? 3 : 1, s), "small-n kernel launch");
+    return QRB_OK;
+  }
+  QRB_TRY(blocked_geqrf(A, H, tau, batch, n, ws, s));
+  return Q != nullptr ? blocked_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
+}
+
+// ---- host-buffer pipeline -------------------------------------------------------
+// The batch is cut into chunks that cycle through kSlots device slots; per chunk the
+// copy-in stream moves A to the slot, the compute stream factors it in place (and
+// forms Q), and the copy-out stream moves H, tau and Q back.  The two copy
+// directions use separate copy engines, so with three slots the host link carries
+// input and output at the same time while the SMs work on a third chunk.
+constexpr int kSlots = 3;
+
+int host_chunks(int64_t batch, int n) {
+  const int k = n <= 128 ? 8 : (n <= 512 ? 4 : 2);
+  return (int)(batch < k ? batch : k);
+}
+
+struct HostPlan {
+  int64_t cb;            // matrices per chunk
+  size_t x_off, t_off, q_off, w_off, slot_bytes, total;
+};
+
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+HostPlan host_plan(int64_t batch, int n, bool with_q) {
+  HostPlan p{};
+  const int k = host_chunks(batch, n);
+  p.cb = k > 0 ? (batch + k - 1) / k : 0;
+  const size_t mat = (size_t)p.cb * n * n * sizeof(float);
+  p.x_off = 0;
+  p.t_off = align256(mat);
+  p.q_off = p.t_off + align256((size_t)p.cb * n * sizeof(float));
+  p.w_off = p.q_off + (with_q ? align256(mat) : 0);
+  p.slot_bytes = p.w_off + align256(ws_bytes(p.cb, n));
+  p.total = p.cb > 0 ? kSlots * p.slot_bytes : 0;
+  return p;
+}
+
+// Internal streams of the host pipeline, one triple per device, created on first use.
+bool pipe_streams(int dev, cudaStream_t (&out)[3]) {
+  static std::mutex mu;
+  static cudaStream_t streams[64][3] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return false;
+  if (streams[dev][0] == nullptr) {
+    cudaStream_t t[3] = {nullptr, nullptr, nullptr};
+    for (auto& x : t)
+      if (cudaStreamCreateWithFlags(&x, cudaStreamNonBlocking) != cudaSuccess) {
+        for (auto y : t)
+          if (y) cudaStreamDestroy(y);
+        cudaGetLastError();
+        return false;
+      }
+    for (int i = 0; i < 3; ++i) streams[dev][i] = t[i];
+  }
+  for (int i = 0; i < 3; ++i) out[i] = streams[dev][i];
+  return true;
+}
+
+struct Events {
+  cudaEvent_t e[3 * kSlots + 1] = {};
+  int made = 0;
+  cudaError_t create() {
+    for (auto& x : e) {
+      cudaError_t r = cudaEventCreateWithFlags(&x, cudaEventDisableTiming);
+      if (r != cudaSuccess) return r;
+      ++made;
+    }
+    return cudaSuccess;
+  }
+  ~Events() {
+    for (int i = 0; i < made; ++i) cudaEventDestroy(e[i]);
+  }
+};
+
+int host_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n, void* dws, size_t dwsb,
+            cudaStream_t s) {
+  const HostPlan p = host_plan(batch, n, Q != nullptr);
+  if (dws == nullptr || dwsb < p.total)
+    return fail(QRB_ERR_WORKSPACE, "device workspace of %zu bytes required, %zu given%s", p.total, dwsb,
+                dws == nullptr ? " (null)" : "");
+  if ((reinterpret_cast<uintptr_t>(dws) & 255u) != 0)
+    return fail(QRB_ERR_INVALID_ARG, "device workspace must be 256-byte aligned");
+  QRB_TRY(check_device());
+  int dev = 0;
+  QRB_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
+  cudaStream_t st[3];
+  if (!pipe_streams(dev, st)) return fail(QRB_ERR_CUDA, "could not create the pipeline streams");
+  Events ev;   // [slot]: copied in, computed, copied out; last: fork
+  QRB_CUDA(ev.create(), "cudaEventCreate");
+  cudaEvent_t* in_ev = ev.e;
+  cudaEvent_t* done_ev = ev.e + kSlots;
+  cudaEvent_t* out_ev = ev.e + 2 * kSlots;
+  cudaEvent_t fork = ev.e[3 * kSlots];
+  QRB_CUDA(cudaEventRecord(fork, s), "cudaEventRecord");
+  for (auto x : st) QRB_CUDA(cudaStreamWaitEvent(x, fork, 0), "cudaStreamWaitEvent");
+  const size_t nn = (size_t)n * n;
+  int chunk = 0;
+  for (int64_t b0 = 0; b0 < batch; b0 += p.cb, ++chunk) {
+    const int64_t cb = batch - b0 < p.cb ? batch - b0 : p.cb;
+    const int slot = chunk % kSlots;
+    char* base = static_cast<char*>(dws) + slot * p.slot_bytes;
+    float* X = reinterpret_cast<float*>(base + p.x_off);
+    float* T = reinterpret_cast<float*>(base + p.t_off);
+    float* Qd = Q != nullptr ? reinterpret_cast<float*>(base + p.q_off) : nullptr;
+    void* W = base + p.w_off;
+    if (chunk >= kSlots) QRB_CUDA(cudaStreamWaitEvent(st[0], out_ev[slot], 0), "cudaStreamWaitEvent");
+    QRB_CUDA(cudaMemcpyAsync(X, A + b0 * nn, cb * nn * sizeof(float), cudaMemcpyHostToDevice, st[0]),
+             "copy-in");
+    QRB_CUDA(cudaEventRecord(in_ev[slot], st[0]), "cudaEventRecord");
+    QRB_CUDA(cudaStreamWaitEvent(st[1], in_ev[slot], 0), "cudaStreamWaitEvent");
+    QRB_TRY(run_qr(X, X, T, Qd, cb, n, W, st[1]));
+    QRB_CUDA(cudaEventRecord(done_ev[slot], st[1]), "cudaEventRecord");
+    QRB_CUDA(cudaStreamWaitEvent(st[2], done_ev[slot], 0), "cudaStreamWaitEvent");
+    QRB_CUDA(cudaMemcpyAsync(H + b0 * nn, X, cb * nn * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
+             "copy-out");
+    QRB_CUDA(cudaMemcpyAsync(tau + b0 * n, T, cb * n * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
+             "copy-out");
+    if (Qd != nullptr)
+      QRB_CUDA(cudaMemcpyAsync(Q + b0 * nn, Qd, cb * nn * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
+               "copy-out");
+    QRB_CUDA(cudaEventRecord(out_ev[slot], st[2]), "cudaEventRecord");
+  }
+  // Join: the copy-out stream is downstream of the other two.
+  QRB_CUDA(cudaEventRecord(fork, st[2]), "cudaEventRecord");
+  QRB_CUDA(cudaStreamWaitEvent(s, fork, 0), "cudaStreamWaitEvent");
+  return QRB_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -215,15 +351,28 @@ int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t batch, in
   QRB_TRY(check_ptr(tau, "tau", false));
   QRB_TRY(check_ptr(Q, "Q"));
   if (Q == H || Q == A) return fail(QRB_ERR_INVALID_ARG, "Q must not alias A or H");
-  if (batch == 0) return QRB_OK;
   QRB_TRY(check_device());
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (n <= qrb::kSmallMaxN) {
-    QRB_CUDA(qrb::launch_small(A, H, tau, Q, batch, n, 3, s), "small-n kernel launch");
-    return QRB_OK;
-  }
-  QRB_TRY(blocked_geqrf(A, H, tau, batch, n, workspace, s));
-  return blocked_orgqr(H, Q, batch, n, workspace, s);
+  return run_qr(A, H, tau, Q, batch, n, workspace, static_cast<cudaStream_t>(stream));
+}
+
+size_t qrb_host_workspace_size(int64_t batch, int n, int with_q) {
+  if (batch < 0 || n < 1 || n > QRB_MAX_N) return 0;
+  return host_plan(batch, n, with_q != 0).total;
+}
+
+int qrb_qr_f32_host(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
+                    void* device_workspace, size_t device_workspace_bytes, void* stream) {
+  if (batch < 0) return fail(QRB_ERR_INVALID_ARG, "batch must be >= 0 (got %lld)", (long long)batch);
+  if (n < 1) return fail(QRB_ERR_INVALID_ARG, "n must be >= 1 (got %d)", n);
+  if (n > QRB_MAX_N) return fail(QRB_ERR_UNSUPPORTED, "n = %d exceeds QRB_MAX_N = %d", n, QRB_MAX_N);
+  if (batch > (int64_t)1 << 31) return fail(QRB_ERR_UNSUPPORTED, "batch = %lld exceeds 2^31", (long long)batch);
+  if (batch == 0) return QRB_OK;
+  if (A == nullptr) return fail(QRB_ERR_INVALID_ARG, "A is null");
+  if (H == nullptr) return fail(QRB_ERR_INVALID_ARG, "H is null");
+  if (tau == nullptr) return fail(QRB_ERR_INVALID_ARG, "tau is null");
+  if (Q != nullptr && (Q == H || Q == A)) return fail(QRB_ERR_INVALID_ARG, "Q must not alias A or H");
+  return host_qr(A, H, tau, Q, batch, n, device_workspace, device_workspace_bytes,
+                 static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

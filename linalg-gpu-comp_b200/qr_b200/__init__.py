@@ -7,7 +7,7 @@ Public API mirrors the reference's submission interface:
 * ``qr(A) -> (H, tau, Q)``              (both, one library call)
 * ``geqrf`` / ``orgqr``                 (aliases with explicit names)
 """
-from .ops import custom_kernel, form_q, geqrf, orgqr, qr  # noqa: F401
+from .ops import custom_kernel, form_q, geqrf, orgqr, qr, qr_host  # noqa: F401
 from ._lib import QRBError, lib  # noqa: F401
 
-__all__ = ["custom_kernel", "form_q", "geqrf", "orgqr", "qr", "QRBError", "lib"]
+__all__ = ["custom_kernel", "form_q", "geqrf", "orgqr", "qr", "qr_host", "QRBError", "lib"]

@@ -31,6 +31,8 @@ SIGNATURES = {
     "qrb_orgqr_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_qr_f32": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_geqrf_f32_noalloc": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp]),
+    "qrb_host_workspace_size": (_c_size, [_c_int64, ctypes.c_int, ctypes.c_int]),
+    "qrb_qr_f32_host": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
 }
 
 _lock = threading.Lock()

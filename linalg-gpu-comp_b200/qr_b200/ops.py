@@ -93,6 +93,41 @@ def qr(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | N
     return H, tau, Q
 
 
+def qr_host(A: torch.Tensor, out: tuple | None = None, with_q: bool = True, device=None):
+    """QR of a HOST batch through one pipelined library call (qrb_qr_f32_host).
+
+    ``A`` is a (batch, n, n) float32 CPU tensor, ideally pinned; returns CPU tensors
+    (H, tau, Q) (Q is None when ``with_q`` is false), pinned when allocated here.
+    Chunks of the batch are copied in, factored and copied out concurrently on the
+    library's internal streams; the call is ordered on torch's current stream of
+    ``device`` (default: the current CUDA device) and is asynchronous like any CUDA
+    work: synchronise that stream before reading the outputs.
+    """
+    if not isinstance(A, torch.Tensor) or A.dtype != torch.float32 or A.dim() != 3 or A.shape[-1] != A.shape[-2]:
+        raise ValueError("A must be a float32 (batch, n, n) tensor")
+    if A.device.type != "cpu":
+        raise ValueError("qr_host takes a host (CPU) tensor; use qr() for device tensors")
+    A = A.contiguous()
+    batch, n, _ = A.shape
+    pin = A.is_pinned()
+    if out is None:
+        H = torch.empty(A.shape, dtype=A.dtype, pin_memory=pin)
+        tau = torch.empty((batch, n), dtype=A.dtype, pin_memory=pin)
+        Q = torch.empty(A.shape, dtype=A.dtype, pin_memory=pin) if with_q else None
+    else:
+        H, tau, Q = out
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        nbytes = int(_lib.lib().qrb_host_workspace_size(batch, n, 1 if Q is not None else 0))
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        _lib.check(_lib.lib().qrb_qr_f32_host(A.data_ptr(), H.data_ptr(), tau.data_ptr(),
+                                              Q.data_ptr() if Q is not None else None, batch, n,
+                                              ws.data_ptr(), nbytes, _queue_handle(dev)))
+        # ws may be released now: the call's internal streams join back into this
+        # stream, which orders any later reuse of the block after them.
+    return H, tau, Q
+
+
 def custom_kernel(data: torch.Tensor):
     """The reference's submission entry point: (H, tau) in torch.geqrf form."""
     return geqrf(data)

@@ -27,7 +27,8 @@ def declared_symbols():
 def test_header_declares_the_api():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
-        "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error"}
+        "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error",
+        "qrb_host_workspace_size", "qrb_qr_f32_host"}
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -100,3 +101,38 @@ def test_python_ops_reject_cpu_and_wrong_dtype():
         custom_kernel(torch.randn(2, 8, 8, dtype=torch.float64).to("meta"))
     with pytest.raises(ValueError):
         form_q(torch.randn(2, 8, 8), torch.randn(2, 8))
+
+
+def test_host_pipeline_workspace_and_argument_checks(lib):
+    """qrb_qr_f32_host: chunked workspace sizing and the checks made before any CUDA call."""
+    def slot(cb, n, with_q):
+        a = lambda x: (x + 255) // 256 * 256
+        mat = a(cb * n * n * 4)
+        return mat + a(cb * n * 4) + (mat if with_q else 0) + a(lib.qrb_workspace_size(cb, n))
+    # n <= 128: 8 chunks; 3 device slots of one chunk each.
+    assert lib.qrb_host_workspace_size(4096, 64, 1) == 3 * slot(512, 64, True)
+    assert lib.qrb_host_workspace_size(4096, 64, 0) == 3 * slot(512, 64, False)
+    assert lib.qrb_host_workspace_size(512, 256, 1) == 3 * slot(128, 256, True)      # 4 chunks
+    assert lib.qrb_host_workspace_size(256, 512, 1) == 3 * slot(64, 512, True)
+    assert lib.qrb_host_workspace_size(32, 2048, 1) == 3 * slot(16, 2048, True)      # 2 chunks
+    assert lib.qrb_host_workspace_size(3, 64, 1) == 3 * slot(1, 64, True)            # batch < chunks
+    assert lib.qrb_host_workspace_size(0, 64, 1) == 0
+    assert lib.qrb_host_workspace_size(4, 0, 1) == 0
+    assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE, None, 0, 64, None, 0, None) == 0   # empty batch
+    assert lib.qrb_qr_f32_host(None, FAKE, FAKE, None, 4, 64, None, 0, None) == 1
+    assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE, FAKE, 4, 64, None, 0, None) == 1   # Q aliases A
+    assert lib.qrb_qr_f32_host(FAKE, FAKE + 64, FAKE + 128, None, 4, 5000, None, 0, None) == 2
+    need = lib.qrb_host_workspace_size(4, 64, 0)
+    assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE + 64, None, 4, 64, FAKE, need - 1, None) == 3
+    assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE + 64, None, 4, 64, FAKE + 16, need, None) == 1
+    st, msg = _err(lib)
+    assert "256-byte" in msg
+
+
+def test_qr_host_rejects_device_and_bad_shapes():
+    import torch
+    from qr_b200 import qr_host
+    with pytest.raises(ValueError):
+        qr_host(torch.randn(2, 8, 7))
+    with pytest.raises(ValueError):
+        qr_host(torch.randn(2, 8, 8, dtype=torch.float64))

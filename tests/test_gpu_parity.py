@@ -252,3 +252,30 @@ def test_no_kernel_recorded_a_wait_timeout():
     """Every bounded device-side wait of the kernels above completed."""
     from qr_b200 import _lib
     assert _lib.lib().qrb_device_error() == 0
+
+
+@pytest.mark.parametrize("batch,n", [(37, 64), (9, 32), (4096, 64), (11, 96), (10, 256), (3, 600), (2, 33)])
+def test_host_pipeline_matches_device_call(batch, n):
+    """qrb_qr_f32_host (pinned host buffers, chunked copy/compute overlap) gives the
+    device call's results bit for bit, with and without Q."""
+    g = torch.Generator(device="cpu").manual_seed(batch * 1000 + n)
+    A_h = torch.randn(batch, n, n, generator=g).pin_memory()
+    H_h, t_h, Q_h = qrb().qr_host(A_h)
+    H2_h, t2_h, none = qrb().qr_host(A_h, with_q=False)
+    torch.cuda.current_stream().synchronize()
+    assert none is None
+    H, tau, Q = qrb().qr(A_h.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(H_h, H.cpu()) and torch.equal(t_h, tau.cpu()) and torch.equal(Q_h, Q.cpu())
+    assert torch.equal(H2_h, H_h) and torch.equal(t2_h, t_h)
+
+
+def test_host_pipeline_in_place_and_pageable():
+    A = torch.randn(20, 64, 64)
+    H_ref, tau_ref, Q_ref = qrb().qr(A.cuda())
+    X = A.clone()                                    # pageable, in place: H overwrites A
+    t = torch.empty(20, 64)
+    Qh = torch.empty(20, 64, 64)
+    qrb().qr_host(X, out=(X, t, Qh))
+    torch.cuda.synchronize()
+    assert torch.equal(X, H_ref.cpu()) and torch.equal(t, tau_ref.cpu()) and torch.equal(Qh, Q_ref.cpu())
