@@ -50,7 +50,7 @@ size_t t_bytes(int64_t batch, int n) {
 size_t ws_bytes(int64_t batch, int n) {
   if (n <= qrb::kSmallMaxN) return 0;
   size_t bytes = t_bytes(batch, n);
-  if (n % 4 == 0) bytes = ((bytes + 255) & ~size_t(255)) + qrb::vprep_floats(batch, n) * sizeof(float);
+  if (n % 4 == 0) bytes = ((bytes + 255) & ~size_t(255)) + qrb::tc_ws_floats(batch, n) * sizeof(float);
   return bytes;
 }
 

@@ -181,7 +181,7 @@ cudaError_t launch_apply(const float* H, const float* T, const float* src, float
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
                          int identity_fill, float* vprep, cudaStream_t s) {
   if (batch == 0 || c0 >= n) return cudaSuccess;
-  if (apply_tc_supported(n))
+  if (vprep != nullptr && apply_tc_supported(n))
     return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, vprep, s);
   return launch_apply_simt(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, s);
 }

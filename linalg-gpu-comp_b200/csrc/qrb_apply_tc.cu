@@ -5,25 +5,25 @@
 // (_wy_trailing_trisolve, submission.py:434-460) and its cublasLt BF16x9 trailing
 // GEMMs (submission.py:875-884).
 //
-// One CTA (4 warps) owns one matrix and a 64-column strip of C over all m rows.
-// V (the panel's unit lower trapezoidal reflectors) is split into its three tf32 pieces
-// once per panel by vprep_kernel and TMA-loaded piece by piece; without that workspace
-// (the allocation-free entry point) each CTA splits V itself.
-//   phase 1  W^T (64 x 32) = C^T V  : TMA streams 32-row stages of C and V into
-//            shared memory (both operands MN-major, which for tf32 takes the 128-byte
-//            swizzle with 32-byte atoms), threads split every value into three
-//            tf32 pieces (x = x0 + x1 + x2), and one thread issues tcgen05.mma
-//            kind::tf32, M=64 N=32 K=8, for the six products of weight >= 2^-22
-//            (x0y0, x0y1, x1y0, x0y2, x1y1, x2y0), issued smallest class first
-//            into one TMEM accumulator per stage; threads sum the stage partials in
-//            fp32 registers.  Together: fp32 accuracy from the tf32 tensor pipe.
-//   phase 2  W2 = op(T) W in registers (fp32), written K-major/swizzled as 3 pieces.
-//   phase 3  per 128-row tile: TMA loads V and C, tcgen05.mma M=128 N=64 K=32 gives
-//            V W2 in TMEM, the epilogue subtracts it from C in shared memory and a
-//            TMA store writes the tile back.
+// fp32 accuracy from the tf32 tensor pipe: every operand is split into three tf32
+// pieces (x = x0 + x1 + x2, vprep_kernel for V, in-kernel for C and W2) and
+// tcgen05.mma kind::tf32 accumulates the six products of weight >= 2^-22 (x0y0,
+// x0y1, x1y0, x0y2, x1y1, x2y0), smallest class first.  Four launches per panel:
+//   vprep_kernel   V (the panel's unit lower trapezoidal reflectors) -> 3 pieces;
+//   wpart_kernel   W^T (64 x 32) = C^T V for a 64-column strip over one row chunk:
+//                  TMA streams 32-row stages of C and V (MN-major operands, which
+//                  for tf32 take the 128-byte swizzle with 32-byte atoms), threads
+//                  split C, one thread issues M=64 N=32 K=8 MMAs into one TMEM
+//                  accumulator per stage, stage partials are summed in registers;
+//   w2_kernel      W = sum of the chunk partials (fixed order), W2 = op(T) W in
+//                  fp32, stored as 3 pieces in the K-major layout of the next step;
+//   update_kernel  C -= V W2 by persistent warp-specialised CTAs: per 128-row
+//                  tile, M=128 N=64 K=32 MMAs into double-buffered TMEM, the
+//                  epilogue subtracts from the TMA-loaded C tile and TMA-stores it.
 // Every mbarrier wait is bounded; a wait that runs out records an error code in
 // g_qrb_device_error and the kernel carries on to its TMEM release and exit.
-// Requires n % 4 == 0 (TMA row strides are multiples of 16 bytes).
+// Requires n % 4 == 0 (TMA row strides are multiples of 16 bytes) and the workspace
+// of tc_ws_floats floats; launch_apply falls back to the SIMT kernel otherwise.
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -39,27 +39,17 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kTN = 64;        // strip width: phase-1 M, phase-3 N
-constexpr int kR1 = 32;        // rows per phase-1 stage
-constexpr int kR3 = 128;       // rows per phase-3 tile (M)
+constexpr int kTN = 64;        // strip width: M of the W^T product, N of the update
+constexpr int kR1 = 32;        // rows per W^T stage
+constexpr int kR3 = 128;       // rows per update tile (M)
 constexpr int kThreads = 128;
-// TMEM: phase 1 uses two stage accumulators x 32 columns, phase 3 one x 64 columns.
-constexpr uint32_t kTmemCols = 64;
 
-// Shared-memory plan (bytes from a 1024-aligned base).  Operands are stored as three
-// tf32 pieces; TMA lands raw fp32 in piece 0, which the split pass overwrites.
+// Shared-memory boxes (fp32, rows of 32 floats = 128 bytes).  TMA lands raw fp32 C in
+// piece 0 of a W^T stage, which the split pass overwrites.
 constexpr int kPieces = 3;
 constexpr uint32_t kBox1 = kR1 * 128;            // 32 rows x 32 floats
 constexpr uint32_t kStage1 = 9 * kBox1;          // C pieces 0..2 (2 boxes each), V pieces 0..2
 constexpr uint32_t kBox3 = kR3 * 128;            // 128 rows x 32 floats
-constexpr uint32_t kOffP3C = 0;                  // phase 3 aliases phase 1
-constexpr uint32_t kOffP3V = 2 * kBox3;          // V pieces at kOffP3V + p * kBox3
-constexpr uint32_t kRegionP = 5 * kBox3;         // 80 KB >= 2 * kStage1 (72 KB)
-constexpr uint32_t kWPiece = kTN * 128;          // W2 piece: 64 rows x 32 floats
-constexpr uint32_t kOffW = kRegionP;
-constexpr uint32_t kOffT = kOffW + kPieces * kWPiece;
-constexpr uint32_t kOffBar = kOffT + 32 * 33 * 4 + 32;
-constexpr uint32_t kSmemBytes = kOffBar + 8 * 8 + 16 + 1024;   // + alignment slack
 
 // The six (A piece, B piece) products kept, smallest first.  The tensor core's fp32
 // accumulation rounds each add relative to the running sum, so all 2^-22 and 2^-11
@@ -69,21 +59,10 @@ constexpr uint32_t kSmemBytes = kOffBar + 8 * 8 + 16 + 1024;   // + alignment sl
 __device__ __constant__ int kTermA[6] = {2, 1, 0, 1, 0, 0};
 __device__ __constant__ int kTermB[6] = {0, 1, 2, 0, 1, 0};
 
-struct Bars {
-  uint64_t tma1[2], mma1[2], tma3, mma3;
-  uint32_t tmem;
-};
-
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_qrb_device_error, 0, code); }
 
 __device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, int code) {
   if (!mbar_wait(bar, parity)) record_error(code);
-}
-
-// V[r][j] of the unit lower trapezoidal block (r relative to the panel top).
-__device__ __forceinline__ float vmask(float x, int r, int j, int b) {
-  if (j >= b) return 0.f;
-  return r > j ? x : (r == j ? 1.f : 0.f);
 }
 
 // Offset of the float4 (row r, columns 4q..4q+3) in the two swizzles.
@@ -126,79 +105,80 @@ __global__ void vprep_kernel(const float* __restrict__ H, float* __restrict__ vp
   }
 }
 
-template <bool PREP, bool IDENT>
-__global__ void __launch_bounds__(kThreads, 1)
-apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_src128,
-                const __grid_constant__ CUtensorMap map_v32, const __grid_constant__ CUtensorMap map_v128,
-                const __grid_constant__ CUtensorMap map_h128, const float* __restrict__ Tg, int64_t batch,
-                int n, int k, int b, int c0, int trans_t, int store_to_h) {
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// ======================================================================================
+// Split update: W^T partials (wpart_kernel) -> W2 = op(T) W in tf32 pieces (w2_kernel)
+// -> C -= V W2 (update_kernel).
+// ======================================================================================
+constexpr int kMaxSplit = 8;            // row chunks of the W^T reduction
+constexpr uint32_t kWBox = kTN * 128;   // W2 piece box: 64 strip columns x 32 floats
+
+// ---- (A) W^T partial over one row chunk: part[split][mat][strip][64][32] -------------
+// Three CTAs per SM: two 36 KB stages; the V pieces come prepared (vprep_kernel).
+constexpr uint32_t kSmemA = 2 * kStage1 + 64 + 1024;
+
+template <bool IDENT>
+__global__ void __launch_bounds__(kThreads, 3)
+wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_v32,
+             float* __restrict__ part, int64_t batch, int n, int k, int b, int c0, int nstrips, int chunk,
+             int nsplit) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
-  Bars& bars = *reinterpret_cast<Bars*>(sm + kOffBar);
-  float (*Ts)[33] = reinterpret_cast<float (*)[33]>(sm + kOffT);
+  uint64_t* tma1 = reinterpret_cast<uint64_t*>(sm + 2 * kStage1);
+  uint64_t* mma1 = tma1 + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma1 + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int nstrips = (n - c0 + kTN - 1) / kTN;
-  const int mat = blockIdx.x / nstrips;
-  const int cs = c0 + (int)(blockIdx.x % nstrips) * kTN;
-  const int m = n - k, kb = k + b;
-  const int nst = (m + kR1 - 1) / kR1;
-  const int ntile = (m + kR3 - 1) / kR3;
-  const int bz = (int)batch;   // z stride between V pieces in the prepared-V maps
+  const int split = blockIdx.x % nsplit;
+  const int t = blockIdx.x / nsplit;
+  const int strip = t % nstrips;
+  const int mat = t / nstrips;
+  const int cs = c0 + strip * kTN;
+  const int r0 = k + split * chunk;
+  const int r1 = min(n, r0 + chunk);
+  const int nst = (r1 - r0 + kR1 - 1) / kR1;   // chunk % 32 == 0: stages never cross chunks
+  const int kb = k + b;
+  const int bz = (int)batch;
 
   if (tid == 0) {
-    mbar_init(&bars.tma1[0], 1);
-    mbar_init(&bars.tma1[1], 1);
-    mbar_init(&bars.mma1[0], 1);
-    mbar_init(&bars.mma1[1], 1);
-    mbar_init(&bars.tma3, 1);
-    mbar_init(&bars.mma3, 1);
+    mbar_init(&tma1[0], 1);
+    mbar_init(&tma1[1], 1);
+    mbar_init(&mma1[0], 1);
+    mbar_init(&mma1[1], 1);
     fence_mbar_init();
     prefetch_tensormap(&map_src32);
     prefetch_tensormap(&map_v32);
   }
-  if (warp == 0) tmem_alloc(&bars.tmem, kTmemCols);
-  // op(T) into shared memory.
-  const float* T = Tg + (size_t)mat * 32 * 32;
-  for (int idx = tid; idx < 32 * 32; idx += kThreads) {
-    const int r = idx >> 5, c = idx & 31;
-    const float t = __ldg(T + idx);
-    if (trans_t) Ts[c][r] = t; else Ts[r][c] = t;
-  }
+  if (warp == 0) tmem_alloc(tslot, 64);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = bars.tmem;
+  const uint32_t tmem = *tslot;
 
   auto issue_stage = [&](int s) {
     unsigned char* st = sm + (s & 1) * kStage1;
-    const int y = k + s * kR1;
-    mbar_arrive_expect_tx(&bars.tma1[s & 1], (PREP ? 5 : 3) * kBox1);
-    tma_load_3d(st, &map_src32, cs, y, mat, &bars.tma1[s & 1]);
-    tma_load_3d(st + kBox1, &map_src32, cs + 32, y, mat, &bars.tma1[s & 1]);
-    if constexpr (PREP) {
+    const int y = r0 + s * kR1;
+    mbar_arrive_expect_tx(&tma1[s & 1], 5 * kBox1);
+    tma_load_3d(st, &map_src32, cs, y, mat, &tma1[s & 1]);
+    tma_load_3d(st + kBox1, &map_src32, cs + 32, y, mat, &tma1[s & 1]);
 #pragma unroll
-      for (int p = 0; p < kPieces; ++p)
-        tma_load_3d(st + (6 + p) * kBox1, &map_v32, 0, y, p * bz + mat, &bars.tma1[s & 1]);
-    } else {
-      tma_load_3d(st + 6 * kBox1, &map_v32, k, y, mat, &bars.tma1[s & 1]);
-    }
+    for (int p = 0; p < kPieces; ++p) tma_load_3d(st + (6 + p) * kBox1, &map_v32, 0, y, p * bz + mat, &tma1[s & 1]);
   };
-
-  // ---------------- phase 1: W^T = C^T V ------------------------------------------
   if (tid == 0) {
     issue_stage(0);
     if (nst > 1) issue_stage(1);
   }
   constexpr uint32_t idesc1 = idesc_tf32(kTN, 32, 1, 1);
-  const uint32_t tm_lane = (uint32_t)(32 * warp) << 16;   // this warp's TMEM lanes
-  float wacc[32];                                          // W^T row (lanes 0-15 meaningful)
+  const uint32_t tm_lane = (uint32_t)(32 * warp) << 16;
+  float wacc[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) wacc[j] = 0.f;
-  // The partial of stage s lives in TMEM columns (s & 1) * 32 ..+32.
   auto gather_stage = [&](int s) {
-    wait_or_flag(&bars.mma1[s & 1], (s >> 1) & 1, 3);
+    wait_or_flag(&mma1[s & 1], (s >> 1) & 1, 13);
     tc_fence_after();
     float p[32];
     tmem_ld32(tmem + tm_lane + (s & 1) * 32, p);
@@ -210,15 +190,14 @@ apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_cons
     const int buf = s & 1;
     const uint32_t par = (s >> 1) & 1;
     unsigned char* st = sm + buf * kStage1;
-    wait_or_flag(&bars.tma1[buf], par, 1);
-    // C: 2 boxes x 32 rows x 8 float4 -> three pieces, piece 0 in place.
+    wait_or_flag(&tma1[buf], par, 11);
     for (int u = tid; u < 2 * kR1 * 8; u += kThreads) {
       const int box = u >> 8, r = (u >> 3) & 31, q = u & 7;
       const uint32_t off = off32b(r, q);
       unsigned char* p0 = st + box * kBox1;
       float4 v = *reinterpret_cast<float4*>(p0 + off);
       if constexpr (IDENT) {
-        const int R = k + s * kR1 + r;
+        const int R = r0 + s * kR1 + r;
         float a[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -229,22 +208,6 @@ apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_cons
       }
       split4_store(p0, 2 * kBox1, off, v);
     }
-    if constexpr (!PREP) {
-      for (int u = tid; u < kR1 * 8; u += kThreads) {
-        const int r = u >> 3, q = u & 7;
-        const uint32_t off = off32b(r, q);
-        unsigned char* p0 = st + 6 * kBox1;
-        float4 v = *reinterpret_cast<float4*>(p0 + off);
-        float a[4] = {v.x, v.y, v.z, v.w};
-        const int rr = s * kR1 + r;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = 4 * q + e;
-          a[e] = rr < 32 ? vmask(a[e], rr, col, b) : (col >= b ? 0.f : a[e]);
-        }
-        split4_store(p0, kBox1, off, make_float4(a[0], a[1], a[2], a[3]));
-      }
-    }
     fence_proxy_async();
     __syncthreads();
     if (tid == 0) {
@@ -252,149 +215,272 @@ apply_tc_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_cons
       const uint32_t base = smem_u32(st);
       const uint32_t d = tmem + buf * 32;
 #pragma unroll
-      for (int t = 0; t < 6; ++t) {
+      for (int tt = 0; tt < 6; ++tt) {
 #pragma unroll
-        for (int kk = 0; kk < kR1 / 8; ++kk) {   // 8 K rows = 1024 bytes per MMA
-          const uint64_t ad = sdesc_sw128_32b(base + 2 * kTermA[t] * kBox1 + kk * 1024, kBox1, 512);
-          const uint64_t bd = sdesc_sw128_32b(base + (6 + kTermB[t]) * kBox1 + kk * 1024, kBox1, 512);
-          mma_tf32(d, ad, bd, idesc1, (t > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kR1 / 8; ++kk) {
+          const uint64_t ad = sdesc_sw128_32b(base + 2 * kTermA[tt] * kBox1 + kk * 1024, kBox1, 512);
+          const uint64_t bd = sdesc_sw128_32b(base + (6 + kTermB[tt]) * kBox1 + kk * 1024, kBox1, 512);
+          mma_tf32(d, ad, bd, idesc1, (tt > 0 || kk > 0) ? 1u : 0u);
         }
       }
-      mma_commit(&bars.mma1[buf]);
+      mma_commit(&mma1[buf]);
     }
-    // Fold the previous stage's partial while this stage's MMAs run, then refill.
     if (s > 0) gather_stage(s - 1);
     __syncthreads();
     if (tid == 0 && s + 2 < nst) {
-      wait_or_flag(&bars.mma1[buf], par, 2);   // MMAs of stage s done reading this buffer
+      wait_or_flag(&mma1[buf], par, 12);
       issue_stage(s + 2);
     }
   }
   gather_stage(nst - 1);
-  tc_fence_after();
-
-  // ---------------- phase 2: W2 = op(T) W  (row i of W^T per lane pair) ---------------
-  {
-    // M = 64 layout: TMEM lanes 0-15 of each warp hold W^T rows 16*warp + lane.
-    float w[32];
+  // M = 64 accumulator: lanes 0-15 of warp w hold W^T rows 16w + lane.
+  if (lane < 16) {
+    const int i = 16 * warp + lane;
+    float4* dst = reinterpret_cast<float4*>(
+        part + ((((size_t)split * batch + mat) * nstrips + strip) * kTN + i) * 32);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) w[j] = __shfl_sync(0xffffffffu, wacc[j], lane & 15);
-    const int i = 16 * warp + (lane & 15);                 // strip column
-    const int a0 = (lane >> 4) * 16;                       // my 16 outputs
-    unsigned char* wp = sm + kOffW;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float o[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int a = a0 + 4 * q + e;
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc = fmaf(Ts[a][j], w[j], acc);
-        o[e] = acc;
-      }
-      split4_store(wp, kWPiece, off128(i, (a0 >> 2) + q), make_float4(o[0], o[1], o[2], o[3]));
-    }
+    for (int q = 0; q < 8; ++q) dst[q] = make_float4(wacc[4 * q], wacc[4 * q + 1], wacc[4 * q + 2], wacc[4 * q + 3]);
   }
   tc_fence_before();
-  fence_proxy_async();
-  __syncthreads();
-  tc_fence_after();
-
-  // ---------------- phase 3: C -= V W2, 128-row tiles -----------------------------------
-  constexpr uint32_t idesc3 = idesc_tf32(kR3, kTN, 0, 0);
-  const CUtensorMap* map_store = store_to_h ? &map_h128 : &map_src128;
-  unsigned char* c3 = sm + kOffP3C;
-  unsigned char* v3 = sm + kOffP3V;
-  for (int t = 0; t < ntile; ++t) {
-    const int y0 = k + t * kR3;
-    if (tid == 0) {
-      if (t > 0) tma_store_wait_read();          // previous tile's store has read c3
-      mbar_arrive_expect_tx(&bars.tma3, (PREP ? 5 : 3) * kBox3);
-      tma_load_3d(c3, &map_src128, cs, y0, mat, &bars.tma3);
-      tma_load_3d(c3 + kBox3, &map_src128, cs + 32, y0, mat, &bars.tma3);
-      if constexpr (PREP) {
-#pragma unroll
-        for (int p = 0; p < kPieces; ++p)
-          tma_load_3d(v3 + p * kBox3, &map_v128, 0, y0, p * bz + mat, &bars.tma3);
-      } else {
-        tma_load_3d(v3, &map_v128, k, y0, mat, &bars.tma3);
-      }
-    }
-    wait_or_flag(&bars.tma3, t & 1, 4);
-    if constexpr (!PREP) {
-      for (int u = tid; u < kR3 * 8; u += kThreads) {
-        const int r = u >> 3, q = u & 7;
-        const uint32_t off = off128(r, q);
-        float4 v = *reinterpret_cast<float4*>(v3 + off);
-        float a[4] = {v.x, v.y, v.z, v.w};
-        const int rr = t * kR3 + r;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = 4 * q + e;
-          a[e] = rr < 32 ? vmask(a[e], rr, col, b) : (col >= b ? 0.f : a[e]);
-        }
-        split4_store(v3, kBox3, off, make_float4(a[0], a[1], a[2], a[3]));
-      }
-      fence_proxy_async();
-    }
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const uint32_t vb = smem_u32(v3), wb = smem_u32(sm + kOffW);
-#pragma unroll
-      for (int t3 = 0; t3 < 6; ++t3) {
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {   // 8 reflectors = 32 bytes per MMA
-          const uint64_t ad = sdesc_sw128(vb + kTermA[t3] * kBox3 + kk * 32, 16, 1024);
-          const uint64_t bd = sdesc_sw128(wb + kTermB[t3] * kWPiece + kk * 32, 16, 1024);
-          mma_tf32(tmem, ad, bd, idesc3, (t3 > 0 || kk > 0) ? 1u : 0u);
-        }
-      }
-      mma_commit(&bars.mma3);
-    }
-    wait_or_flag(&bars.mma3, t & 1, 5);
-    tc_fence_after();
-    // Epilogue: row 32*warp + lane of the tile.
-    {
-      const int r = 32 * warp + lane;
-      const int R = y0 + r;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        float d[32];
-        tmem_ld32(tmem + tm_lane + 32 * half, d);
-        unsigned char* box = c3 + half * kBox3;
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint32_t off = off128(r, q);
-          float4 c = *reinterpret_cast<float4*>(box + off);
-          float cv[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if constexpr (IDENT) {
-              const int Cc = cs + 32 * half + 4 * q + e;
-              if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
-            }
-            cv[e] -= d[4 * q + e];
-          }
-          *reinterpret_cast<float4*>(box + off) = make_float4(cv[0], cv[1], cv[2], cv[3]);
-        }
-      }
-    }
-    tc_fence_before();
-    fence_proxy_async();
-    __syncthreads();
-    if (tid == 0) {
-      tma_store_3d(map_store, c3, cs, y0, mat);
-      tma_store_3d(map_store, c3 + kBox3, cs + 32, y0, mat);
-      tma_store_commit();
-    }
-  }
-  if (tid == 0) tma_store_wait_all();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    tmem_dealloc(tmem, kTmemCols);
+    tmem_dealloc(tmem, 64);
+  }
+}
+
+// ---- (A2) W2 = op(T) W, summed over the row chunks in a fixed order ------------------
+// w2[p][mat][col][a] (col = absolute column, a = reflector): the K-major B operand of
+// update_kernel, split into three tf32 pieces.
+__global__ void __launch_bounds__(256)
+w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* __restrict__ w2, int64_t batch,
+          int n, int c0, int nstrips, int nsplit, int trans_t) {
+  __shared__ float Ts[32][33];
+  __shared__ float Ws[kTN][33];
+  const int strip = blockIdx.x % nstrips;
+  const int mat = blockIdx.x / nstrips;
+  const int cs = c0 + strip * kTN;
+  const float* T = Tg + (size_t)mat * 32 * 32;
+  for (int idx = threadIdx.x; idx < 32 * 32; idx += blockDim.x) {
+    const int r = idx >> 5, c = idx & 31;
+    const float t = __ldg(T + idx);
+    if (trans_t) Ts[c][r] = t; else Ts[r][c] = t;
+  }
+  for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
+    const int i = idx >> 5, j = idx & 31;
+    float w = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp)
+      w += __ldg(part + ((((size_t)sp * batch + mat) * nstrips + strip) * kTN + i) * 32 + j);
+    Ws[i][j] = w;
+  }
+  __syncthreads();
+  const size_t piece = (size_t)batch * n * 32;
+  for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
+    const int i = idx >> 5, a = idx & 31;   // strip column, reflector
+    if (cs + i >= n) continue;
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) acc = fmaf(Ts[a][j], Ws[i][j], acc);
+    float x0, x1, x2;
+    split3_tf32(acc, x0, x1, x2);
+    const size_t o = ((size_t)mat * n + cs + i) * 32 + a;
+    w2[o] = x0;
+    w2[piece + o] = x1;
+    w2[2 * piece + o] = x2;
+  }
+}
+
+// ---- (B) C -= V W2: persistent CTAs over (matrix, 128-row tile, strip group) items ---
+// Warp roles: 0 = TMA producer, 1 = MMA issuer (and TMEM owner), 2-5 = epilogue (warp w
+// reads TMEM lanes 32*(w%4).., i.e. tile rows 32*(w%4)+lane).  An item's V pieces stay
+// in shared memory for its strips; each strip's W2 pieces and C tile go through a ring
+// of kSlotsB slots; two TMEM accumulators let the MMAs of one strip run under the
+// epilogue of the previous one.  Ring positions and parities run on a per-CTA strip
+// counter across items, so the pipeline does not drain between items (only the V
+// reload waits for the previous item's last MMA).
+constexpr int kSlotsB = 3;
+constexpr int kThreadsB = 192;
+constexpr uint32_t kOffBV = 0;                              // V pieces: 3 x 16 KB
+constexpr uint32_t kSlotW = 0;                              // in a slot: W2 pieces 3 x 8 KB
+constexpr uint32_t kSlotC = kPieces * kWBox;                // then C: 2 boxes x 16 KB
+constexpr uint32_t kSlotBytes = kSlotC + 2 * kBox3;         // 56 KB
+constexpr uint32_t kOffBSlots = kPieces * kBox3;            // 48 KB
+constexpr uint32_t kOffBBar = kOffBSlots + kSlotsB * kSlotBytes;
+constexpr uint32_t kSmemB = kOffBBar + 128 + 1024;
+
+struct BarsB {
+  uint64_t full[kSlotsB], empty[kSlotsB], vfull, vempty, accf[2], acce[2];
+  uint32_t tmem;
+};
+
+struct ItemB {
+  int mat, y0, s0, s1;   // matrix, first tile row, strip range [s0, s1)
+};
+
+__device__ __forceinline__ ItemB item_b(int64_t item, int k, int ntiles, int ngroups, int gsize, int nstrips) {
+  ItemB it;
+  const int g = (int)(item % ngroups);
+  const int64_t t = item / ngroups;
+  it.y0 = k + (int)(t % ntiles) * kR3;
+  it.mat = (int)(t / ntiles);
+  it.s0 = g * gsize;
+  it.s1 = min(nstrips, it.s0 + gsize);
+  return it;
+}
+
+template <bool IDENT>
+__global__ void __launch_bounds__(kThreadsB, 1)
+update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_constant__ CUtensorMap map_h128,
+              const __grid_constant__ CUtensorMap map_v128, const __grid_constant__ CUtensorMap map_w,
+              int64_t batch, int n, int k, int b, int c0, int nstrips, int ntiles, int ngroups, int gsize,
+              int store_to_h) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  BarsB& bars = *reinterpret_cast<BarsB*>(sm + kOffBBar);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb = k + b;
+  const int bz = (int)batch;
+  const int64_t nitems = batch * ntiles * ngroups;
+
+  if (tid == 0) {
+    for (int i = 0; i < kSlotsB; ++i) {
+      mbar_init(&bars.full[i], 1);
+      mbar_init(&bars.empty[i], 1);
+    }
+    mbar_init(&bars.vfull, 1);
+    mbar_init(&bars.vempty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.accf[i], 1);
+      mbar_init(&bars.acce[i], 4);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars.tmem, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&map_src128);
+      prefetch_tensormap(&map_w);
+      prefetch_tensormap(&map_v128);
+      int gs = 0, iter = 0;
+      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+        const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
+        if (iter > 0) wait_or_flag(&bars.vempty, (iter - 1) & 1, 20);   // last MMA of the previous item
+        mbar_arrive_expect_tx(&bars.vfull, kPieces * kBox3);
+#pragma unroll
+        for (int p = 0; p < kPieces; ++p)
+          tma_load_3d(sm + kOffBV + p * kBox3, &map_v128, 0, it.y0, p * bz + it.mat, &bars.vfull);
+        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+          const int slot = gs % kSlotsB, use = gs / kSlotsB;
+          if (use > 0) wait_or_flag(&bars.empty[slot], (use - 1) & 1, 21);
+          unsigned char* sl = sm + kOffBSlots + slot * kSlotBytes;
+          const int cs = c0 + s * kTN;
+          mbar_arrive_expect_tx(&bars.full[slot], kPieces * kWBox + 2 * kBox3);
+#pragma unroll
+          for (int p = 0; p < kPieces; ++p)
+            tma_load_3d(sl + kSlotW + p * kWBox, &map_w, 0, cs, p * bz + it.mat, &bars.full[slot]);
+          tma_load_3d(sl + kSlotC, &map_src128, cs, it.y0, it.mat, &bars.full[slot]);
+          tma_load_3d(sl + kSlotC + kBox3, &map_src128, cs + 32, it.y0, it.mat, &bars.full[slot]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc3 = idesc_tf32(kR3, kTN, 0, 0);
+      const uint32_t vb = smem_u32(sm + kOffBV);
+      int gs = 0, iter = 0;
+      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+        const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
+        wait_or_flag(&bars.vfull, iter & 1, 22);
+        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+          const int slot = gs % kSlotsB, acc = gs & 1;
+          wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 23);
+          if (gs >= 2) wait_or_flag(&bars.acce[acc], ((gs >> 1) - 1) & 1, 24);
+          tc_fence_after();
+          const uint32_t wb = smem_u32(sm + kOffBSlots + slot * kSlotBytes + kSlotW);
+          const uint32_t d = tmem + acc * kTN;
+#pragma unroll
+          for (int t3 = 0; t3 < 6; ++t3) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = sdesc_sw128(vb + kTermA[t3] * kBox3 + kk * 32, 16, 1024);
+              const uint64_t bd = sdesc_sw128(wb + kTermB[t3] * kWBox + kk * 32, 16, 1024);
+              mma_tf32(d, ad, bd, idesc3, (t3 > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&bars.accf[acc]);
+        }
+        mma_commit(&bars.vempty);   // V of this item no longer read once these complete
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2-5) ----------------
+    const int q = warp & 3;
+    const int r = 32 * q + lane;   // tile row
+    const CUtensorMap* map_store = store_to_h ? &map_h128 : &map_src128;
+    const bool leader = (warp == 2 && lane == 0);
+    int gs = 0;
+    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
+      const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
+      const int R = it.y0 + r;
+      for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        const int slot = gs % kSlotsB, acc = gs & 1;
+        const int cs = c0 + s * kTN;
+        unsigned char* cbox = sm + kOffBSlots + slot * kSlotBytes + kSlotC;
+        wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 25);
+        wait_or_flag(&bars.accf[acc], (gs >> 1) & 1, 26);
+        tc_fence_after();
+        float d[2][32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * kTN, d[0]);
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * kTN + 32, d[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.acce[acc]);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          unsigned char* box = cbox + half * kBox3;
+#pragma unroll
+          for (int qq = 0; qq < 8; ++qq) {
+            const uint32_t off = off128(r, qq);
+            float4 c = *reinterpret_cast<float4*>(box + off);
+            float cv[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if constexpr (IDENT) {
+                const int Cc = cs + 32 * half + 4 * qq + e;
+                if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+              }
+              cv[e] -= d[half][4 * qq + e];
+            }
+            *reinterpret_cast<float4*>(box + off) = make_float4(cv[0], cv[1], cv[2], cv[3]);
+          }
+        }
+        fence_proxy_async();
+        named_bar_sync(1, 128);
+        if (leader) {
+          tma_store_3d(map_store, cbox, cs, it.y0, it.mat);
+          if (cs + 32 < n) tma_store_3d(map_store, cbox + kBox3, cs + 32, it.y0, it.mat);
+          tma_store_commit();
+          // The store of the previous strip has finished reading its slot: hand it back.
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          if (gs > 0) mbar_arrive(&bars.empty[(gs - 1) % kSlotsB]);
+        }
+      }
+    }
+    if (leader) tma_store_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 128);
   }
 }
 
@@ -427,68 +513,100 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows,
   return r == CUDA_SUCCESS;
 }
 
-template <bool PREP, bool IDENT>
-cudaError_t launch_t(const CUtensorMap& s32, const CUtensorMap& s128, const CUtensorMap& v32,
-                     const CUtensorMap& v128, const CUtensorMap& h128, const float* T, int64_t batch, int n,
-                     int k, int b, int c0, int trans_t, int store_to_h, cudaStream_t st) {
+}  // namespace
+
+bool apply_tc_supported(int n) { return n % 4 == 0 && n >= 64 && encode_fn() != nullptr; }
+
+// Tensor-core workspace: V pieces and W2 pieces ([piece][batch][n][32] each), then
+// the W^T partials ([split][batch][strip][64][32]).
+size_t tc_ws_floats(int64_t batch, int n) {
+  return (size_t)2 * kPieces * batch * n * 32 + (size_t)kMaxSplit * batch * ((n + kTN - 1) / kTN) * kTN * 32;
+}
+
+namespace {
+
+template <bool IDENT>
+cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const CUtensorMap& s128,
+                         const CUtensorMap& h128, const CUtensorMap& v128, const CUtensorMap& w, const float* T,
+                         float* part, float* w2, int64_t batch, int n, int k, int b, int c0, int trans_t,
+                         int store_to_h, cudaStream_t st) {
   static std::atomic<unsigned long long> attr_done{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const unsigned long long bit = 1ull << (dev & 63);
   if (!(attr_done.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(apply_tc_kernel<PREP, IDENT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kSmemBytes);
+    e = cudaFuncSetAttribute(wpart_kernel<IDENT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemA);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(update_kernel<IDENT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemB);
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  const unsigned grid = (unsigned)((int64_t)((n - c0 + kTN - 1) / kTN) * batch);
-  apply_tc_kernel<PREP, IDENT><<<grid, kThreads, kSmemBytes, st>>>(s32, s128, v32, v128, h128, T, batch, n, k,
-                                                                   b, c0, trans_t, store_to_h);
+  const int m = n - k;
+  const int nstrips = (n - c0 + kTN - 1) / kTN;
+  const int ntiles = (m + kR3 - 1) / kR3;
+  // Row chunks for the W^T reduction: enough CTAs for ~2 waves at 3 per SM.
+  const int64_t units = (int64_t)nstrips * batch;
+  int nsplit = (int)((888 + units - 1) / units);
+  nsplit = nsplit < 1 ? 1 : (nsplit > kMaxSplit ? kMaxSplit : nsplit);
+  const int max_split = (m + 63) / 64;   // at least two 32-row stages per chunk
+  if (nsplit > max_split) nsplit = max_split < 1 ? 1 : max_split;
+  int chunk = (m + nsplit - 1) / nsplit;
+  chunk = (chunk + kR1 - 1) / kR1 * kR1;
+  nsplit = (m + chunk - 1) / chunk;
+  wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(s32, v32, part, batch, n, k, b, c0,
+                                                                            nstrips, chunk, nsplit);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  w2_kernel<<<(unsigned)units, 256, 0, st>>>(part, T, w2, batch, n, c0, nstrips, nsplit, trans_t);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // Persistent update: at least four items per SM so the last round is short; strip
+  // groups (each reloading V) only when there are too few row tiles for that.
+  const int64_t tiles = batch * ntiles;
+  int ngroups = (int)((4 * 148 + tiles - 1) / tiles);
+  ngroups = ngroups < 1 ? 1 : (ngroups > nstrips ? nstrips : ngroups);
+  const int gsize = (nstrips + ngroups - 1) / ngroups;
+  ngroups = (nstrips + gsize - 1) / gsize;
+  const int64_t items = tiles * ngroups;
+  const unsigned gridb = (unsigned)(items < 148 ? items : 148);
+  update_kernel<IDENT><<<gridb, kThreadsB, kSmemB, st>>>(s128, h128, v128, w, batch, n, k, b, c0, nstrips, ntiles,
+                                                         ngroups, gsize, store_to_h);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-bool apply_tc_supported(int n) { return n % 4 == 0 && n >= 64 && encode_fn() != nullptr; }
-
-size_t vprep_floats(int64_t batch, int n) { return (size_t)kPieces * batch * n * 32; }
-
 cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C, int64_t batch,
-                            int n, int k, int b, int c0, int trans_t, int identity_fill, float* vprep,
+                            int n, int k, int b, int c0, int trans_t, int identity_fill, float* tcws,
                             cudaStream_t s) {
   if (batch == 0 || c0 >= n) return cudaSuccess;
+  if (tcws == nullptr) return cudaErrorInvalidValue;
   const int store_to_h = (C == H) ? 1 : 0;
   if (!store_to_h && C != src) return cudaErrorInvalidValue;   // C is either H or the source
-  // Phase-1 boxes feed MN-major operands (32-byte-atom swizzle); phase-3 boxes are
-  // K-major operands and the epilogue tile (plain 128-byte swizzle).
-  const CUtensorMapSwizzle sw1 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, sw3 = CU_TENSOR_MAP_SWIZZLE_128B;
-  CUtensorMap m_s32, m_s128, m_v32, m_v128, m_h128;
-  if (!make_map(&m_s32, src, n, n, batch, kR1, sw1) || !make_map(&m_s128, src, n, n, batch, kR3, sw3) ||
-      !make_map(&m_h128, H, n, n, batch, kR3, sw3))
-    return cudaErrorInvalidValue;
-  if (vprep != nullptr) {
+  float* vprep = tcws;
+  float* w2 = vprep + (size_t)kPieces * batch * n * 32;
+  float* part = w2 + (size_t)kPieces * batch * n * 32;
+  {
     const int64_t total = batch * (int64_t)(n - k) * 32;
     const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
     vprep_kernel<<<blocks, 256, 0, s>>>(H, vprep, batch, n, k, b);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (!make_map(&m_v32, vprep, 32, n, kPieces * batch, kR1, sw1) ||
-        !make_map(&m_v128, vprep, 32, n, kPieces * batch, kR3, sw3))
-      return cudaErrorInvalidValue;
-    return identity_fill
-               ? launch_t<true, true>(m_s32, m_s128, m_v32, m_v128, m_h128, T, batch, n, k, b, c0, trans_t,
-                                      store_to_h, s)
-               : launch_t<true, false>(m_s32, m_s128, m_v32, m_v128, m_h128, T, batch, n, k, b, c0, trans_t,
-                                       store_to_h, s);
   }
-  if (!make_map(&m_v32, H, n, n, batch, kR1, sw1) || !make_map(&m_v128, H, n, n, batch, kR3, sw3))
+  // 32-row boxes feed MN-major operands (32-byte-atom swizzle); 128-row boxes are
+  // K-major operands and the epilogue tile (plain 128-byte swizzle).
+  const CUtensorMapSwizzle sw1 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, sw3 = CU_TENSOR_MAP_SWIZZLE_128B;
+  CUtensorMap m_s32, m_s128, m_v32, m_v128, m_h128, m_w;
+  if (!make_map(&m_s32, src, n, n, batch, kR1, sw1) || !make_map(&m_s128, src, n, n, batch, kR3, sw3) ||
+      !make_map(&m_h128, H, n, n, batch, kR3, sw3) || !make_map(&m_v32, vprep, 32, n, kPieces * batch, kR1, sw1) ||
+      !make_map(&m_v128, vprep, 32, n, kPieces * batch, kR3, sw3) ||
+      !make_map(&m_w, w2, 32, n, kPieces * batch, kTN, sw3))
     return cudaErrorInvalidValue;
-  return identity_fill
-             ? launch_t<false, true>(m_s32, m_s128, m_v32, m_v128, m_h128, T, batch, n, k, b, c0, trans_t,
-                                     store_to_h, s)
-             : launch_t<false, false>(m_s32, m_s128, m_v32, m_v128, m_h128, T, batch, n, k, b, c0, trans_t,
-                                      store_to_h, s);
+  return identity_fill ? launch_split<true>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
+                                            b, c0, trans_t, store_to_h, s)
+                       : launch_split<false>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
+                                             b, c0, trans_t, store_to_h, s);
 }
 
 int take_device_error() {

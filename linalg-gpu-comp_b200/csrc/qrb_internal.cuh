@@ -70,12 +70,13 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T,
 // (Q_k^T, the geqrf trailing update), 0 applies T (Q_k, orgqr).  `src` is read
 // (it may equal C).  If identity_fill, entries of C with row < k+b or column < k+b
 // are taken as the identity instead of being read (orgqr without a Q init).
-// `vprep` (nullable): workspace of vprep_floats(batch, n) floats for the three tf32
-// pieces of V, prepared once per call so the tensor-core kernel's CTAs need not split V.
+// `vprep` (nullable): workspace of tc_ws_floats(batch, n) floats for the tensor-core
+// path (tf32 pieces of V and of W2, and the W^T partials); without it, or for
+// n % 4 != 0, the SIMT kernel runs.
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
                          int identity_fill, float* vprep, cudaStream_t s);
-size_t vprep_floats(int64_t batch, int n);
+size_t tc_ws_floats(int64_t batch, int n);
 
 // The two implementations launch_apply dispatches to (SIMT fp32 for any n).
 cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, float* C,

@@ -15,6 +15,9 @@
 //     (32 x 32 fp32 = 4 KiB per matrix), so for n > 64 the batch may be at most
 //     kNoAllocScratchBytes / 4 KiB = 2048 matrices.  n <= 64 needs no scratch
 //     and has no batch limit.  Larger batches are rejected (QRB_ERR_UNSUPPORTED).
+//   * For n > 64 the trailing updates run on the SIMT fp32 kernel (qrb_apply.cu):
+//     the tensor-core path needs workspace for its split operands.  Results agree
+//     with the regular entry point to fp32 rounding, not bit for bit.
 //   * Every GPU that loads the library holds the 8 MiB array until process exit.
 //   * Every call shares the one array.  Each panel writes its T block in full
 //     before the trailing update reads it, so nothing has to be cleared between
