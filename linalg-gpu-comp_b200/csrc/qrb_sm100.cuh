@@ -175,21 +175,24 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 }
 
 // ---- split-precision helpers ----------------------------------------------------------
+// fp32 -> tf32 (10 explicit mantissa bits), round to nearest with ties away from zero:
+// add half a tf32 unit in the last place to the magnitude bits and clear the 13 low
+// bits.  Integer ALU work, so the conversion does not queue on the slower conversion
+// pipe; for finite x it equals cvt.rna.tf32.f32.
 __device__ __forceinline__ float tf32_rn(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// x = x0 + x1 + x2 with every piece representable in tf32 (round to nearest at each
-// step; the remainder after x2 is below 2^-33 |x|).  With the six products
-// x0y0 + x0y1 + x1y0 + x0y2 + x1y1 + x2y0 a tf32 tensor-core product carries about
-// 24 bits, i.e. fp32 accuracy.
+// x = x0 + x1 + x2 with every piece representable in tf32: x0 = rn(x); r = x - x0 is
+// exact and keeps at most the 13 low significand bits of x; x1 = rn(r); x2 = r - x1 is
+// exact and has at most 2 significant bits, so it is a tf32 value as it stands.  With
+// the six products x0y0 + x0y1 + x1y0 + x0y2 + x1y1 + x2y0 a tf32 tensor-core product
+// carries about 24 bits, i.e. fp32 accuracy.
 __device__ __forceinline__ void split3_tf32(float x, float& x0, float& x1, float& x2) {
   x0 = tf32_rn(x);
   const float r = x - x0;
   x1 = tf32_rn(r);
-  x2 = tf32_rn(r - x1);
+  x2 = r - x1;
 }
 
 // Byte offset of logical (row, col) of fp32 tile whose rows are 128 bytes (32 floats)
