@@ -59,12 +59,13 @@ def kernel_launches(n: int) -> int:
         return 1
     np_ = (n + 31) // 32
     applies = (np_ - 1) + np_         # trailing updates + orgqr blocks
-    vsplits = applies if n % 4 == 0 else 0   # tensor-core path: one V split per update
-    return np_ + applies + vsplits
+    # tensor-core path (n % 4 == 0): V split, W^T partials, W2, update per block
+    per_apply = 4 if n % 4 == 0 else 1
+    return np_ + applies * per_apply
 
 
 def dominant_kernel(n: int) -> str:
-    return "small_qr_kernel" if n <= 64 else "apply_kernel"
+    return "small_qr_kernel" if n <= 64 else "wpart_kernel"
 
 
 def load_peaks() -> dict:

@@ -52,5 +52,6 @@ def test_bench_accounting():
     assert bench.bytes_per_matrix(64) == 12 * 64 * 64 + 4 * 64
     assert bench.flops_per_matrix(3) == pytest.approx(72.0)
     assert bench.kernel_launches(64) == 1
-    # n = 256: 8 panels, 7 trailing updates, 8 orgqr blocks, plus one V split per update
-    assert bench.kernel_launches(256) == 8 + 7 + 8 + 15
+    # n = 256: 8 panels, 7 trailing updates, 8 orgqr blocks
+    assert bench.kernel_launches(256) == 8 + (7 + 8) * 4          # panels + 4 launches per tensor-core update
+    assert bench.kernel_launches(258) == 9 + (8 + 9)              # n % 4 != 0: one SIMT launch per update
