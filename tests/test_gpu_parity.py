@@ -279,3 +279,51 @@ def test_host_pipeline_in_place_and_pageable():
     qrb().qr_host(X, out=(X, t, Qh))
     torch.cuda.synchronize()
     assert torch.equal(X, H_ref.cpu()) and torch.equal(t, tau_ref.cpu()) and torch.equal(Qh, Q_ref.cpu())
+
+
+# ---------------------------------------------------------------------------
+# the device checker (qr_b200.checker) against the reference's own checker values
+# ---------------------------------------------------------------------------
+_CHK_KEYS = ("scaled_factor_residual", "scaled_reconstruction_residual",
+             "scaled_triangular_residual", "scaled_orthogonality_residual")
+
+
+@pytest.mark.parametrize("name,case", golden_cases())
+def test_device_checker_matches_reference_checker(golden, name, case):
+    """The golden fixtures hold the residuals the reference's check_implementation
+    printed for the reference's own v1 output (Q from torch householder_product on
+    CPU).  The device checker (Q from qrb_orgqr_f32) must reach the same verdict and
+    the same residuals up to the rounding of the two fp32 Q formations: each scaled
+    residual within 0.25 + 50% of the reference's value (they are O(1e-2..1) numbers
+    in units of n·eps·scale)."""
+    from qr_b200.checker import check_implementation, residuals
+    A = torch.from_numpy(golden[f"{name}/A"]).cuda()
+    H = torch.from_numpy(golden[f"{name}/H_v1"]).cuda()
+    tau = torch.from_numpy(golden[f"{name}/tau_v1"]).cuda()
+    ok, msg = check_implementation(A, (H, tau))
+    assert ok, msg
+    res = residuals(A, H, tau)
+    ref = golden[f"{name}/chk_v1"]
+    for key, r in zip(_CHK_KEYS, ref):
+        assert abs(res[key] - r) <= 0.25 + 0.5 * abs(r), (key, res[key], r)
+
+
+def test_device_checker_rejects_bad_outputs():
+    from qr_b200.checker import check_implementation
+    A = torch.randn(4, 96, 96, device="cuda")
+    H, tau = qrb().custom_kernel(A)
+    assert check_implementation(A, (H, tau))[0]
+    bad_tau = tau.clone()
+    bad_tau[1, 5] *= 1.5
+    ok, msg = check_implementation(A, (H, bad_tau))
+    assert not ok and ("orthogonal" in msg or "R - Q.T" in msg)
+    bad_h = H.clone()
+    bad_h[2, 0, 3] += 1.0
+    ok, msg = check_implementation(A, (bad_h, tau))
+    assert not ok and "R - Q.T" in msg
+    ok, msg = check_implementation(A, (H, tau[:, :-1]))
+    assert not ok and "shape" in msg
+    nan_h = H.clone()
+    nan_h[0, 0, 0] = float("nan")
+    ok, msg = check_implementation(A, (nan_h, tau))
+    assert not ok and "NaN" in msg
