@@ -59,8 +59,8 @@ def kernel_launches(n: int) -> int:
         return 1
     np_ = (n + 31) // 32
     applies = (np_ - 1) + np_         # trailing updates + orgqr blocks
-    # tensor-core path (n % 4 == 0): V split, W^T partials, W2, update per block
-    per_apply = 4 if n % 4 == 0 else 1
+    # tensor-core path (n % 4 == 0): W^T partials, W2, update per block
+    per_apply = 3 if n % 4 == 0 else 1
     return np_ + applies * per_apply
 
 

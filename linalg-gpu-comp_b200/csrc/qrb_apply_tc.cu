@@ -5,18 +5,18 @@
 // (_wy_trailing_trisolve, submission.py:434-460) and its cublasLt BF16x9 trailing
 // GEMMs (submission.py:875-884).
 //
-// fp32 accuracy from the tf32 tensor pipe: every operand is split into three tf32
-// pieces (x = x0 + x1 + x2, vprep_kernel for V, in-kernel for C and W2) and
-// tcgen05.mma kind::tf32 accumulates the six products of weight >= 2^-22 (x0y0,
-// x0y1, x1y0, x0y2, x1y1, x2y0), smallest class first.  Four launches per panel:
-//   vprep_kernel   V (the panel's unit lower trapezoidal reflectors) -> 3 pieces;
+// fp32 accuracy from the tf32 tensor pipe: every operand is split in shared memory
+// into three tf32 pieces (x = x0 + x1 + x2) and tcgen05.mma kind::tf32 accumulates
+// the six products of weight >= 2^-22 (x0y0, x0y1, x1y0, x0y2, x1y1, x2y0), smallest
+// class first.  Operands travel through HBM as plain fp32 (V straight from H, masked to
+// the unit lower trapezoid where it is split).  Three launches per panel:
 //   wpart_kernel   W^T (64 x 32) = C^T V for a 64-column strip over one row chunk:
 //                  TMA streams 32-row stages of C and V (MN-major operands, which
 //                  for tf32 take the 128-byte swizzle with 32-byte atoms), threads
-//                  split C, one thread issues M=64 N=32 K=8 MMAs into one TMEM
+//                  split both, one thread issues M=64 N=32 K=8 MMAs into one TMEM
 //                  accumulator per stage, stage partials are summed in registers;
-//   w2_kernel      W = sum of the chunk partials (fixed order), W2 = op(T) W in
-//                  fp32, stored as 3 pieces in the K-major layout of the next step;
+//   w2_kernel      W = sum of the chunk partials (fixed order), W2 = op(T) W in fp32,
+//                  in the K-major layout of the next step;
 //   update_kernel  C -= V W2 by persistent warp-specialised CTAs: per 128-row
 //                  tile, M=128 N=64 K=32 MMAs into double-buffered TMEM, the
 //                  epilogue subtracts from the TMA-loaded C tile and TMA-stores it.
@@ -65,6 +65,12 @@ __device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, int
   if (!mbar_wait(bar, parity)) record_error(code);
 }
 
+// V[r][j] of the unit lower trapezoidal block (r relative to the panel top).
+__device__ __forceinline__ float vmask(float x, int r, int j, int b) {
+  if (j >= b) return 0.f;
+  return r > j ? x : (r == j ? 1.f : 0.f);
+}
+
 // Offset of the float4 (row r, columns 4q..4q+3) in the two swizzles.
 __device__ __forceinline__ uint32_t off32b(int r, int q) {
   return r * 128u + (((((uint32_t)q >> 1) ^ (uint32_t)r) & 3u) << 5) + ((uint32_t)(q & 1) << 4);
@@ -82,47 +88,21 @@ __device__ __forceinline__ void split4_store(unsigned char* p0, uint32_t pstride
   *reinterpret_cast<float4*>(p0 + 2 * pstride + off) = make_float4(x2[0], x2[1], x2[2], x2[3]);
 }
 
-// V pieces of one panel: vp[p][mat][row][32], rows k..n-1 written (masked V, 3 tf32 pieces).
-__global__ void vprep_kernel(const float* __restrict__ H, float* __restrict__ vp, int64_t batch, int n,
-                             int k, int b) {
-  const int m = n - k;
-  const int64_t total = batch * (int64_t)m * 32;
-  const size_t piece = (size_t)batch * n * 32;
-  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
-       e += (int64_t)gridDim.x * blockDim.x) {
-    const int c = (int)(e & 31);
-    const int64_t t = e >> 5;
-    const int r = (int)(t % m);
-    const int64_t mat = t / m;
-    float x = 0.f;
-    if (c < b) x = r > c ? __ldg(H + (size_t)mat * n * n + (size_t)(k + r) * n + k + c) : (r == c ? 1.f : 0.f);
-    float x0, x1, x2;
-    split3_tf32(x, x0, x1, x2);
-    const size_t o = ((size_t)mat * n + k + r) * 32 + c;
-    vp[o] = x0;
-    vp[piece + o] = x1;
-    vp[2 * piece + o] = x2;
-  }
-}
-
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
-// ======================================================================================
-// Split update: W^T partials (wpart_kernel) -> W2 = op(T) W in tf32 pieces (w2_kernel)
-// -> C -= V W2 (update_kernel).
-// ======================================================================================
 constexpr int kMaxSplit = 8;            // row chunks of the W^T reduction
 constexpr uint32_t kWBox = kTN * 128;   // W2 piece box: 64 strip columns x 32 floats
 
 // ---- (A) W^T partial over one row chunk: part[split][mat][strip][64][32] -------------
-// Three CTAs per SM: two 36 KB stages; the V pieces come prepared (vprep_kernel).
+// Three CTAs per SM: two 36 KB stages.  V arrives raw from H (masked to the unit lower
+// trapezoid here) and is split with C.
 constexpr uint32_t kSmemA = 2 * kStage1 + 64 + 1024;
 
 template <bool IDENT>
 __global__ void __launch_bounds__(kThreads, 3)
-wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_v32,
+wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_hv32,
              float* __restrict__ part, int64_t batch, int n, int k, int b, int c0, int nstrips, int chunk,
              int nsplit) {
   extern __shared__ unsigned char smem_raw[];
@@ -142,7 +122,6 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   const int r1 = min(n, r0 + chunk);
   const int nst = (r1 - r0 + kR1 - 1) / kR1;   // chunk % 32 == 0: stages never cross chunks
   const int kb = k + b;
-  const int bz = (int)batch;
 
   if (tid == 0) {
     mbar_init(&tma1[0], 1);
@@ -151,7 +130,7 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
     mbar_init(&mma1[1], 1);
     fence_mbar_init();
     prefetch_tensormap(&map_src32);
-    prefetch_tensormap(&map_v32);
+    prefetch_tensormap(&map_hv32);
   }
   if (warp == 0) tmem_alloc(tslot, 64);
   tc_fence_before();
@@ -162,11 +141,10 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   auto issue_stage = [&](int s) {
     unsigned char* st = sm + (s & 1) * kStage1;
     const int y = r0 + s * kR1;
-    mbar_arrive_expect_tx(&tma1[s & 1], 5 * kBox1);
+    mbar_arrive_expect_tx(&tma1[s & 1], 3 * kBox1);
     tma_load_3d(st, &map_src32, cs, y, mat, &tma1[s & 1]);
     tma_load_3d(st + kBox1, &map_src32, cs + 32, y, mat, &tma1[s & 1]);
-#pragma unroll
-    for (int p = 0; p < kPieces; ++p) tma_load_3d(st + (6 + p) * kBox1, &map_v32, 0, y, p * bz + mat, &tma1[s & 1]);
+    tma_load_3d(st + 6 * kBox1, &map_hv32, k, y, mat, &tma1[s & 1]);
   };
   if (tid == 0) {
     issue_stage(0);
@@ -207,6 +185,22 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
         v = make_float4(a[0], a[1], a[2], a[3]);
       }
       split4_store(p0, 2 * kBox1, off, v);
+    }
+    // V: rows of the stage relative to the panel top; the first 32 hold the unit
+    // upper part of the reflectors (1 on the diagonal, 0 above), the rest is H as is.
+    for (int u = tid; u < kR1 * 8; u += kThreads) {
+      const int r = u >> 3, q = u & 7;
+      const uint32_t off = off32b(r, q);
+      unsigned char* p0 = st + 6 * kBox1;
+      float4 v = *reinterpret_cast<float4*>(p0 + off);
+      const int rr = r0 + s * kR1 + r - k;
+      if (rr < 32) {
+        float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a[e] = vmask(a[e], rr, 4 * q + e, b);
+        v = make_float4(a[0], a[1], a[2], a[3]);
+      }
+      split4_store(p0, kBox1, off, v);
     }
     fence_proxy_async();
     __syncthreads();
@@ -250,8 +244,8 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
 }
 
 // ---- (A2) W2 = op(T) W, summed over the row chunks in a fixed order ------------------
-// w2[p][mat][col][a] (col = absolute column, a = reflector): the K-major B operand of
-// update_kernel, split into three tf32 pieces.
+// w2[mat][col][a] (col = absolute column, a = reflector), fp32: the K-major B operand of
+// update_kernel, which splits it into tf32 pieces in shared memory.
 __global__ void __launch_bounds__(256)
 w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* __restrict__ w2, int64_t batch,
           int n, int c0, int nstrips, int nsplit, int trans_t) {
@@ -274,42 +268,37 @@ w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* _
     Ws[i][j] = w;
   }
   __syncthreads();
-  const size_t piece = (size_t)batch * n * 32;
   for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
     const int i = idx >> 5, a = idx & 31;   // strip column, reflector
     if (cs + i >= n) continue;
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) acc = fmaf(Ts[a][j], Ws[i][j], acc);
-    float x0, x1, x2;
-    split3_tf32(acc, x0, x1, x2);
-    const size_t o = ((size_t)mat * n + cs + i) * 32 + a;
-    w2[o] = x0;
-    w2[piece + o] = x1;
-    w2[2 * piece + o] = x2;
+    w2[((size_t)mat * n + cs + i) * 32 + a] = acc;
   }
 }
 
 // ---- (B) C -= V W2: persistent CTAs over (matrix, 128-row tile, strip group) items ---
 // Warp roles: 0 = TMA producer, 1 = MMA issuer (and TMEM owner), 2-5 = epilogue (warp w
-// reads TMEM lanes 32*(w%4).., i.e. tile rows 32*(w%4)+lane).  An item's V pieces stay
-// in shared memory for its strips; each strip's W2 pieces and C tile go through a ring
-// of kSlotsB slots; two TMEM accumulators let the MMAs of one strip run under the
+// reads TMEM lanes 32*(w%4).., i.e. tile rows 32*(w%4)+lane), 6-9 = converters, which
+// split the raw fp32 V tile (from H, masked to the unit lower trapezoid) and each
+// strip's raw W2 into tf32 pieces in place.  An item's V pieces stay in shared memory
+// for its strips; each strip's W2 and C tile go through a ring of kSlotsB slots; two TMEM accumulators let the MMAs of one strip run under the
 // epilogue of the previous one.  Ring positions and parities run on a per-CTA strip
 // counter across items, so the pipeline does not drain between items (only the V
 // reload waits for the previous item's last MMA).
 constexpr int kSlotsB = 3;
-constexpr int kThreadsB = 192;
+constexpr int kThreadsB = 320;
 constexpr uint32_t kOffBV = 0;                              // V pieces: 3 x 16 KB
 constexpr uint32_t kSlotW = 0;                              // in a slot: W2 pieces 3 x 8 KB
 constexpr uint32_t kSlotC = kPieces * kWBox;                // then C: 2 boxes x 16 KB
 constexpr uint32_t kSlotBytes = kSlotC + 2 * kBox3;         // 56 KB
 constexpr uint32_t kOffBSlots = kPieces * kBox3;            // 48 KB
 constexpr uint32_t kOffBBar = kOffBSlots + kSlotsB * kSlotBytes;
-constexpr uint32_t kSmemB = kOffBBar + 128 + 1024;
+constexpr uint32_t kSmemB = kOffBBar + 160 + 1024;
 
 struct BarsB {
-  uint64_t full[kSlotsB], empty[kSlotsB], vfull, vempty, accf[2], acce[2];
+  uint64_t full[kSlotsB], empty[kSlotsB], w2ready[kSlotsB], vfull, vready, vempty, accf[2], acce[2];
   uint32_t tmem;
 };
 
@@ -331,7 +320,7 @@ __device__ __forceinline__ ItemB item_b(int64_t item, int k, int ntiles, int ngr
 template <bool IDENT>
 __global__ void __launch_bounds__(kThreadsB, 1)
 update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_constant__ CUtensorMap map_h128,
-              const __grid_constant__ CUtensorMap map_v128, const __grid_constant__ CUtensorMap map_w,
+              const __grid_constant__ CUtensorMap map_hv128, const __grid_constant__ CUtensorMap map_w,
               int64_t batch, int n, int k, int b, int c0, int nstrips, int ntiles, int ngroups, int gsize,
               int store_to_h) {
   extern __shared__ unsigned char smem_raw[];
@@ -340,15 +329,16 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
   BarsB& bars = *reinterpret_cast<BarsB*>(sm + kOffBBar);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int kb = k + b;
-  const int bz = (int)batch;
   const int64_t nitems = batch * ntiles * ngroups;
 
   if (tid == 0) {
     for (int i = 0; i < kSlotsB; ++i) {
       mbar_init(&bars.full[i], 1);
       mbar_init(&bars.empty[i], 1);
+      mbar_init(&bars.w2ready[i], 4);
     }
     mbar_init(&bars.vfull, 1);
+    mbar_init(&bars.vready, 4);
     mbar_init(&bars.vempty, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bars.accf[i], 1);
@@ -367,24 +357,20 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
     if (lane == 0) {
       prefetch_tensormap(&map_src128);
       prefetch_tensormap(&map_w);
-      prefetch_tensormap(&map_v128);
+      prefetch_tensormap(&map_hv128);
       int gs = 0, iter = 0;
       for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
         const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
         if (iter > 0) wait_or_flag(&bars.vempty, (iter - 1) & 1, 20);   // last MMA of the previous item
-        mbar_arrive_expect_tx(&bars.vfull, kPieces * kBox3);
-#pragma unroll
-        for (int p = 0; p < kPieces; ++p)
-          tma_load_3d(sm + kOffBV + p * kBox3, &map_v128, 0, it.y0, p * bz + it.mat, &bars.vfull);
+        mbar_arrive_expect_tx(&bars.vfull, kBox3);
+        tma_load_3d(sm + kOffBV, &map_hv128, k, it.y0, it.mat, &bars.vfull);
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kSlotsB, use = gs / kSlotsB;
           if (use > 0) wait_or_flag(&bars.empty[slot], (use - 1) & 1, 21);
           unsigned char* sl = sm + kOffBSlots + slot * kSlotBytes;
           const int cs = c0 + s * kTN;
-          mbar_arrive_expect_tx(&bars.full[slot], kPieces * kWBox + 2 * kBox3);
-#pragma unroll
-          for (int p = 0; p < kPieces; ++p)
-            tma_load_3d(sl + kSlotW + p * kWBox, &map_w, 0, cs, p * bz + it.mat, &bars.full[slot]);
+          mbar_arrive_expect_tx(&bars.full[slot], kWBox + 2 * kBox3);
+          tma_load_3d(sl + kSlotW, &map_w, 0, cs, it.mat, &bars.full[slot]);
           tma_load_3d(sl + kSlotC, &map_src128, cs, it.y0, it.mat, &bars.full[slot]);
           tma_load_3d(sl + kSlotC + kBox3, &map_src128, cs + 32, it.y0, it.mat, &bars.full[slot]);
         }
@@ -398,10 +384,10 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
       int gs = 0, iter = 0;
       for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
         const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
-        wait_or_flag(&bars.vfull, iter & 1, 22);
+        wait_or_flag(&bars.vready, iter & 1, 22);
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kSlotsB, acc = gs & 1;
-          wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 23);
+          wait_or_flag(&bars.w2ready[slot], (gs / kSlotsB) & 1, 23);
           if (gs >= 2) wait_or_flag(&bars.acce[acc], ((gs >> 1) - 1) & 1, 24);
           tc_fence_after();
           const uint32_t wb = smem_u32(sm + kOffBSlots + slot * kSlotBytes + kSlotW);
@@ -418,6 +404,48 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
           mma_commit(&bars.accf[acc]);
         }
         mma_commit(&bars.vempty);   // V of this item no longer read once these complete
+      }
+    }
+  } else if (warp >= 6) {
+    // ---------------- converters (warps 6-9) ----------------
+    const int ct = tid - 192;   // 0..127
+    int gs = 0, iter = 0;
+    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+      const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
+      wait_or_flag(&bars.vfull, iter & 1, 27);
+      // V tile: 128 rows x 8 float4; rows relative to the panel top below 32 are masked.
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i) {
+        const int u = ct + 128 * i;
+        const int r = u >> 3, q = u & 7;
+        const uint32_t off = off128(r, q);
+        unsigned char* p0 = sm + kOffBV;
+        float4 v = *reinterpret_cast<float4*>(p0 + off);
+        const int rr = it.y0 - k + r;
+        if (rr < 32) {
+          float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) a[e] = vmask(a[e], rr, 4 * q + e, b);
+          v = make_float4(a[0], a[1], a[2], a[3]);
+        }
+        split4_store(p0, kBox3, off, v);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.vready);
+      for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        const int slot = gs % kSlotsB;
+        wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 28);
+        unsigned char* p0 = sm + kOffBSlots + slot * kSlotBytes + kSlotW;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {   // W2: 64 rows x 8 float4
+          const int u = ct + 128 * i;
+          const uint32_t off = off128(u >> 3, u & 7);
+          split4_store(p0, kWBox, off, *reinterpret_cast<float4*>(p0 + off));
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.w2ready[slot]);
       }
     }
   } else {
@@ -517,10 +545,10 @@ bool make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows,
 
 bool apply_tc_supported(int n) { return n % 4 == 0 && n >= 64 && encode_fn() != nullptr; }
 
-// Tensor-core workspace: V pieces and W2 pieces ([piece][batch][n][32] each), then
-// the W^T partials ([split][batch][strip][64][32]).
+// Tensor-core workspace: W2 ([batch][n][32] fp32), then the W^T partials
+// ([split][batch][strip][64][32]).
 size_t tc_ws_floats(int64_t batch, int n) {
-  return (size_t)2 * kPieces * batch * n * 32 + (size_t)kMaxSplit * batch * ((n + kTN - 1) / kTN) * kTN * 32;
+  return (size_t)batch * n * 32 + (size_t)kMaxSplit * batch * ((n + kTN - 1) / kTN) * kTN * 32;
 }
 
 namespace {
@@ -584,24 +612,15 @@ cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, fl
   if (tcws == nullptr) return cudaErrorInvalidValue;
   const int store_to_h = (C == H) ? 1 : 0;
   if (!store_to_h && C != src) return cudaErrorInvalidValue;   // C is either H or the source
-  float* vprep = tcws;
-  float* w2 = vprep + (size_t)kPieces * batch * n * 32;
-  float* part = w2 + (size_t)kPieces * batch * n * 32;
-  {
-    const int64_t total = batch * (int64_t)(n - k) * 32;
-    const unsigned blocks = (unsigned)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    vprep_kernel<<<blocks, 256, 0, s>>>(H, vprep, batch, n, k, b);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
-  }
+  float* w2 = tcws;
+  float* part = w2 + (size_t)batch * n * 32;
   // 32-row boxes feed MN-major operands (32-byte-atom swizzle); 128-row boxes are
   // K-major operands and the epilogue tile (plain 128-byte swizzle).
   const CUtensorMapSwizzle sw1 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, sw3 = CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap m_s32, m_s128, m_v32, m_v128, m_h128, m_w;
   if (!make_map(&m_s32, src, n, n, batch, kR1, sw1) || !make_map(&m_s128, src, n, n, batch, kR3, sw3) ||
-      !make_map(&m_h128, H, n, n, batch, kR3, sw3) || !make_map(&m_v32, vprep, 32, n, kPieces * batch, kR1, sw1) ||
-      !make_map(&m_v128, vprep, 32, n, kPieces * batch, kR3, sw3) ||
-      !make_map(&m_w, w2, 32, n, kPieces * batch, kTN, sw3))
+      !make_map(&m_h128, H, n, n, batch, kR3, sw3) || !make_map(&m_v32, H, n, n, batch, kR1, sw1) ||
+      !make_map(&m_v128, H, n, n, batch, kR3, sw3) || !make_map(&m_w, w2, 32, n, batch, kTN, sw3))
     return cudaErrorInvalidValue;
   return identity_fill ? launch_split<true>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
                                             b, c0, trans_t, store_to_h, s)

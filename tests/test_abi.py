@@ -47,10 +47,10 @@ def test_version_and_status_strings(lib):
 
 @pytest.mark.parametrize("batch,n,expect", [
     (10, 1, 0), (10, 64, 0), (10, 65, 3 * 10 * 32 * 32 * 4),
-    # T factors + (n % 4 == 0) V and W2 pieces (3 each) + 8 row-chunk W^T partials
-    (7, 512, 16 * 7 * 4096 + (6 + 8) * 7 * 512 * 32 * 4),
-    (32, 2048, 64 * 32 * 4096 + (6 + 8) * 32 * 2048 * 32 * 4),
-    (3, 100, 4 * 3 * 4096 + (6 * 3 * 100 * 32 + 8 * 3 * 128 * 32) * 4),
+    # T factors + (n % 4 == 0) W2 (fp32) + 8 row-chunk W^T partials
+    (7, 512, 16 * 7 * 4096 + (1 + 8) * 7 * 512 * 32 * 4),
+    (32, 2048, 64 * 32 * 4096 + (1 + 8) * 32 * 2048 * 32 * 4),
+    (3, 100, 4 * 3 * 4096 + (3 * 100 * 32 + 8 * 3 * 128 * 32) * 4),
     (1, 4097, 0), (-1, 100, 0)])
 def test_workspace_size(lib, batch, n, expect):
     assert lib.qrb_workspace_size(batch, n) == expect
