@@ -5,7 +5,10 @@ input and output pointers, or a path that must not enter the allocator -- use
 this entry point; its scratch is a static device array inside the library.  The
 test calls it through the C ABI twice in a row (the second call sees the scratch
 the first one left behind) and compares each result with the regular
-qrb_geqrf_f32, within the H/tau tolerance of the other parity tests.  This file
+qrb_geqrf_f32.  The two run different fp32 trailing updates (SIMT here, the
+tensor-core split kernels there), so their rounding differs like two LAPACK
+builds': the H/tau tolerance of the other parity tests, 5e-5, is scaled by n/256
+beyond n = 256 (rounding differences grow with the number of panels).  This file
 sorts last so a stop-at-first-failure run has already run every other test.
 """
 import ctypes
@@ -59,8 +62,9 @@ def test_noalloc_matches_regular_twice(lib, batch, n):
         H, tau = _noalloc(lib, A)
         torch.cuda.synchronize()
         scale = A.abs().max().item()
-        assert (H - H_ref).abs().max().item() <= TOL_H * scale, call
-        assert (tau - tau_ref).abs().max().item() <= TOL_H, call
+        tol = TOL_H * max(1.0, n / 256)
+        assert (H - H_ref).abs().max().item() <= tol * scale, call
+        assert (tau - tau_ref).abs().max().item() <= tol, call
 
 
 def test_noalloc_rejects_batch_beyond_scratch(lib):
