@@ -327,3 +327,29 @@ def test_device_checker_rejects_bad_outputs():
     nan_h[0, 0, 0] = float("nan")
     ok, msg = check_implementation(A, (nan_h, tau))
     assert not ok and "NaN" in msg
+
+
+@pytest.mark.parametrize("n", [48, 200])
+def test_cuda_graph_capture_and_replay(n):
+    """The device entry points launch only on the caller's stream and allocate nothing,
+    so a QR can be captured into a CUDA graph (workspace and outputs from the graph's
+    pool) and replayed on new inputs copied into the captured input buffer."""
+    A = torch.randn(6, n, n, device="cuda")
+    qrb().qr(A)                                   # first-use setup outside the capture
+    torch.cuda.synchronize()
+    static_A = A.clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            H_g, tau_g, Q_g = qrb().qr(static_A)
+    torch.cuda.current_stream().wait_stream(s)
+    for seed in range(2):
+        B = torch.randn(6, n, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(seed))
+        static_A.copy_(B)
+        g.replay()
+        torch.cuda.synchronize()
+        H, tau, Q = qrb().qr(B)
+        torch.cuda.synchronize()
+        assert torch.equal(H_g, H) and torch.equal(tau_g, tau) and torch.equal(Q_g, Q)
