@@ -5,11 +5,12 @@
 //   n <= 64  : one fused CTA per matrix (qrb_small.cu) -- geqrf and Q in one launch.
 //   n >  64  : right-looking blocked Householder, panel width 32:
 //                for each panel k: panel geqr2 + T (qrb_panel.cu), then the
-//                trailing update A[k:, k+32:] -= V T^T V^T A (qrb_apply.cu);
+//                trailing update A[k:, k+32:] -= V T^T V^T A (qrb_apply_tc.cu on
+//                the tensor cores for n % 4 == 0, qrb_apply.cu otherwise);
 //              Q by backward block accumulation Q[k:, k:] -= V T V^T Q[k:, k:]
 //              over the same T factors, with the identity generated on the fly.
 // Workspace: the T factors of every panel, [panel][batch][32][32] fp32, then the
-// tf32 pieces of one panel's V for the tensor-core update (see ws_bytes).
+// tensor-core update's scratch (see ws_bytes).
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -46,7 +47,7 @@ size_t t_bytes(int64_t batch, int n) {
 }
 
 // Workspace: the T factors of every panel, then (for the tensor-core path, n % 4 == 0)
-// one panel's V split into three tf32 pieces, [piece][batch][n][32] fp32.
+// the update's scratch: W2 and the row-chunk partials of W^T (qrb::tc_ws_floats).
 size_t ws_bytes(int64_t batch, int n) {
   if (n <= qrb::kSmallMaxN) return 0;
   size_t bytes = t_bytes(batch, n);
@@ -54,7 +55,7 @@ size_t ws_bytes(int64_t batch, int n) {
   return bytes;
 }
 
-float* vprep_ws(void* ws, int64_t batch, int n) {
+float* tc_ws(void* ws, int64_t batch, int n) {
   if (n % 4 != 0) return nullptr;
   return reinterpret_cast<float*>(static_cast<char*>(ws) + ((t_bytes(batch, n) + 255) & ~size_t(255)));
 }
@@ -124,7 +125,7 @@ int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, vo
     float* T = panel_T(ws, batch, p);
     QRB_CUDA(qrb::launch_panel(src, H, tau, T, batch, n, k, b, s), "panel kernel launch");
     if (k + b < n)
-      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, vprep_ws(ws, batch, n), s), "trailing update launch");
+      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, tc_ws(ws, batch, n), s), "trailing update launch");
   }
   return QRB_OK;
 }
@@ -132,7 +133,7 @@ int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, vo
 int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
   for (int p = n_panels(n) - 1; p >= 0; --p) {
     const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
-    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, vprep_ws(ws, batch, n), s),
+    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, tc_ws(ws, batch, n), s),
              "orgqr block launch");
   }
   return QRB_OK;

@@ -179,10 +179,10 @@ apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const fl
 
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
-                         int identity_fill, float* vprep, cudaStream_t s) {
+                         int identity_fill, float* tcws, cudaStream_t s) {
   if (batch == 0 || c0 >= n) return cudaSuccess;
-  if (vprep != nullptr && apply_tc_supported(n))
-    return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, vprep, s);
+  if (tcws != nullptr && apply_tc_supported(n))
+    return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, tcws, s);
   return launch_apply_simt(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, s);
 }
 

@@ -48,7 +48,7 @@ constexpr int kThreads = 128;
 // piece 0 of a W^T stage, which the split pass overwrites.
 constexpr int kPieces = 3;
 constexpr uint32_t kBox1 = kR1 * 128;            // 32 rows x 32 floats
-constexpr uint32_t kStage1 = 9 * kBox1;          // C pieces 0..2 (2 boxes each), V pieces 0..2
+constexpr uint32_t kStage1 = 9 * kBox1;          // C pieces 0..2 (2 boxes each), then V pieces 0..2
 constexpr uint32_t kBox3 = kR3 * 128;            // 128 rows x 32 floats
 
 // The six (A piece, B piece) products kept, smallest first.  The tensor core's fp32

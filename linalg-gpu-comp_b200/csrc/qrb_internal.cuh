@@ -70,12 +70,12 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T,
 // (Q_k^T, the geqrf trailing update), 0 applies T (Q_k, orgqr).  `src` is read
 // (it may equal C).  If identity_fill, entries of C with row < k+b or column < k+b
 // are taken as the identity instead of being read (orgqr without a Q init).
-// `vprep` (nullable): workspace of tc_ws_floats(batch, n) floats for the tensor-core
+// `tcws` (nullable): workspace of tc_ws_floats(batch, n) floats for the tensor-core
 // path (tf32 pieces of V and of W2, and the W^T partials); without it, or for
 // n % 4 != 0, the SIMT kernel runs.
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
                          int64_t batch, int n, int k, int b, int c0, int trans_t,
-                         int identity_fill, float* vprep, cudaStream_t s);
+                         int identity_fill, float* tcws, cudaStream_t s);
 size_t tc_ws_floats(int64_t batch, int n);
 
 // The two implementations launch_apply dispatches to (SIMT fp32 for any n).
@@ -86,7 +86,7 @@ cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, 
 bool apply_tc_supported(int n);
 cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C,
                             int64_t batch, int n, int k, int b, int c0, int trans_t,
-                            int identity_fill, float* vprep, cudaStream_t s);
+                            int identity_fill, float* tcws, cudaStream_t s);
 
 // First error code recorded by a kernel whose bounded wait ran out (0 = none); clears it.
 int take_device_error();
