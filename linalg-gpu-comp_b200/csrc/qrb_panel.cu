@@ -36,9 +36,12 @@ __global__ void __launch_bounds__(kPanelThreads)
 panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __restrict__ tau,
              float* __restrict__ Tout, int n, int k, int b) {
   constexpr int kRowsCta = kPanelWarps * RPT;
-  __shared__ float2 red_n[2][CL * kPanelWarps];   // (tail^2, alpha) partials
-  __shared__ float red_w[2][kPanelWarps][32];     // per-warp w partials
-  __shared__ float red_c[2][CL][32];              // per-CTA w partials (CL > 1)
+  __shared__ float2 red_n[2][kPanelWarps];        // per-warp (tail^2, alpha) partials
+  __shared__ float red_w[2][kPanelWarps][32];     // per-warp d_c partials
+  __shared__ float rowj[2][32];                   // row j of the panel (rank 0)
+  __shared__ float2 cred_n[2][CL];                // per-CTA partials (CL > 1)
+  __shared__ float cred_w[2][CL][32];
+  __shared__ float crowj[2][32];
   __shared__ float Ts[32][33];                    // T factor (rank 0 only)
   __shared__ float Gs[32][33];                    // strict upper part of V^T V (rank 0)
   __shared__ float taus[32];
@@ -71,76 +74,84 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   float my_inv = 1.f, my_beta = 0.f;   // this lane's column reflector (set at step j == lane)
   for (int j = 0; j < b; ++j) {
     const int par = j & 1;
-    // ---- 1. column j of my rows, partial norms --------------------------------
+    // ---- 1. column j of my rows: partial ||x||^2 and alpha, and for every column c
+    //         d_c = sum over rows r > j of x_r a_rc, which does not depend on the
+    //         reflector: u^T a_c = v0 a_jc + d_c.  So one reduction round per step.
     float u[RPT];
-    float tail = 0.f, tail2 = 0.f, alpha = 0.f;
+    float tail = 0.f, tail2 = 0.f, alpha = 0.f, d0 = 0.f, d1 = 0.f, ajc = 0.f;
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
       const int pr = row0 + 8 * i;
       const float x = __shfl_sync(0xffffffffu, a[i], j);
       u[i] = x;
       if (i < kTop) {
-        tail += pr > j ? x * x : 0.f;
+        const float xt = pr > j ? x : 0.f;
+        tail = fmaf(xt, xt, tail);
         alpha += pr == j ? x : 0.f;
+        ajc += pr == j ? a[i] : 0.f;
+        d0 = fmaf(xt, a[i], d0);
       } else if (i & 1) {
         tail2 = fmaf(x, x, tail2);
+        d1 = fmaf(x, a[i], d1);
       } else {
         tail = fmaf(x, x, tail);
+        d0 = fmaf(x, a[i], d0);
       }
     }
     tail += tail2;
-    // ---- 2. combine (tail^2, alpha) -------------------------------------------
-    if constexpr (CL == 1) {
-      if (lane == 0) red_n[par][warp] = make_float2(tail, alpha);
-      __syncthreads();
-    } else {
-      auto cluster = cg::this_cluster();
-      if (lane < CL) {
-        float2* dst = cluster.map_shared_rank(&red_n[par][rank * kPanelWarps + warp], lane);
-        *dst = make_float2(tail, alpha);
-      }
-      cluster.sync();
-    }
-    {
-      // CL * 8 partials (up to 64): lane l folds slots l, l + 32, ... then a butterfly.
-      float2 p = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int q = lane; q < CL * kPanelWarps; q += 32) {
-        const float2 t = red_n[par][q];
-        p.x += t.x;
-        p.y += t.y;
-      }
-      tail = warp_sum(p.x);
-      alpha = warp_sum(p.y);
-    }
-    const Reflector f = make_reflector(alpha, tail, j == m - 1);
-
-    // ---- 3. w_c = u^T a_c (= v0 * v^T a_c) --------------------------------------
-    float wp = 0.f, wp2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < RPT; ++i) {
-      const int pr = row0 + 8 * i;
-      if (i < kTop) u[i] = pr > j ? u[i] : (pr == j ? f.v0 : 0.f);
-      if (i & 1) wp2 = fmaf(u[i], a[i], wp2); else wp = fmaf(u[i], a[i], wp);
-    }
-    red_w[par][warp][lane] = wp + wp2;
+    // ---- 2. one reduction round (double-buffered: one barrier per step suffices) ----
+    if (lane == 0) red_n[par][warp] = make_float2(tail, alpha);
+    red_w[par][warp][lane] = d0 + d1;
+    if (rank == 0 && warp == (j & (kPanelWarps - 1))) rowj[par][lane] = ajc;   // row j: warp j % 8
     __syncthreads();
-    float w = 0.f;
+    float2 nsum = make_float2(0.f, 0.f);
+    float dsum = 0.f, aj;
     if constexpr (CL == 1) {
 #pragma unroll
-      for (int q = 0; q < kPanelWarps; ++q) w += red_w[par][q][lane];
+      for (int q = 0; q < kPanelWarps; ++q) {
+        const float2 t = red_n[par][q];
+        nsum.x += t.x;
+        nsum.y += t.y;
+        dsum += red_w[par][q][lane];
+      }
+      aj = rowj[par][lane];
     } else {
+      // CTA sums first, then every rank receives all CL of them through distributed
+      // shared memory and adds them in rank order (bit-identical beta / tau everywhere).
       auto cluster = cg::this_cluster();
       if (warp == 0) {
-        float s = 0.f;
+        float2 p = make_float2(0.f, 0.f);
+        float sw = 0.f;
 #pragma unroll
-        for (int q = 0; q < kPanelWarps; ++q) s += red_w[par][q][lane];
+        for (int q = 0; q < kPanelWarps; ++q) {
+          const float2 t = red_n[par][q];
+          p.x += t.x;
+          p.y += t.y;
+          sw += red_w[par][q][lane];
+        }
 #pragma unroll
-        for (int q = 0; q < CL; ++q) *cluster.map_shared_rank(&red_c[par][rank][lane], q) = s;
+        for (int q = 0; q < CL; ++q) {
+          *cluster.map_shared_rank(&cred_w[par][rank][lane], q) = sw;
+          if (lane == 0) *cluster.map_shared_rank(&cred_n[par][rank], q) = p;
+          if (rank == 0) *cluster.map_shared_rank(&crowj[par][lane], q) = rowj[par][lane];
+        }
       }
       cluster.sync();
 #pragma unroll
-      for (int q = 0; q < CL; ++q) w += red_c[par][q][lane];
+      for (int q = 0; q < CL; ++q) {
+        const float2 t = cred_n[par][q];
+        nsum.x += t.x;
+        nsum.y += t.y;
+        dsum += cred_w[par][q][lane];
+      }
+      aj = crowj[par][lane];
+    }
+    const Reflector f = make_reflector(nsum.y, nsum.x, j == m - 1);
+    const float w = fmaf(f.v0, aj, dsum);   // u^T a_c with u = (0.., v0, x_{j+1}, ..)
+#pragma unroll
+    for (int i = 0; i < kTop && i < RPT; ++i) {
+      const int pr = row0 + 8 * i;
+      u[i] = pr > j ? u[i] : (pr == j ? f.v0 : 0.f);
     }
 
     // ---- 4. apply to columns > j (lane j keeps its raw column) -------------------
