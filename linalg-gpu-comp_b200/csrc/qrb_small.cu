@@ -7,7 +7,8 @@
 // (reference_repo/reference.py:144).
 //
 // Layout.  NP (32 or 64) is n rounded up.  Four lanes share a column: lane =
-// 8*rg + cl (rg in 0..3) of warp w owns columns 16w + cl and 16w + 8 + cl and the
+// 8*rg + cl (rg in 0..3) of warp w owns two columns -- 16w + cl and 16w + 8 + cl for
+// NP = 64, w + 2cl and w + 2cl + 16 for NP = 32 (see SmallCfg::kCyclic) -- and the
 // rows {rg + 4i}, all in registers, so the CTA has NP/16 warps (small register
 // footprint per matrix: more matrices in flight per SM).  A column reduction over rows is a
 // register sum plus two xor shuffles (8, 16).
@@ -40,6 +41,13 @@ struct SmallCfg {
   static constexpr int kR = NP / kRG;    // rows per lane
   static constexpr int kB = kR / 4;      // float4 blocks per lane (4*kRG matrix rows each)
   static constexpr int kBlockRows = 4 * kRG;
+  // Column ownership.  Cyclic (warp w owns columns w, w + kWarps, ..): every warp keeps
+  // work to the last step and each step's update is spread over all warps -- shorter
+  // steps, more issued instructions; measured faster for n <= 32 (latency-bound, few
+  // matrices) and slower for n = 64.  Blocked (warp w owns 16 consecutive columns):
+  // warps retire as the factorisation passes them.
+  static constexpr bool kCyclic = NP == 32;
+  static constexpr int kKKStep = kCyclic ? 8 * kWarps : 8;      // between a lane's kk columns
 };
 
 __device__ __forceinline__ void named_barrier(int id, int count) {
@@ -112,13 +120,16 @@ template <int NP, int B0>
 __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][SmallCfg<NP>::kR], int j,
                                            int n, int rg, int col0, bool pivot, Reflector (&mine)[kCPL]) {
   constexpr int kB = SmallCfg<NP>::kB;
+  constexpr int kKK = SmallCfg<NP>::kKKStep;
+  // cyclic ownership: column blocks kk < kKmin lie left of row block B0 (all done)
+  constexpr int kKmin = SmallCfg<NP>::kCyclic ? 2 * B0 / SmallCfg<NP>::kWarps : 0;
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
   float d[kCPL];
 #pragma unroll
-  for (int kk = 0; kk < kCPL; ++kk) {
+  for (int kk = kKmin; kk < kCPL; ++kk) {
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -130,10 +141,10 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
     d[kk] = (d0 + d1) + (d2 + d3);
   }
 #pragma unroll
-  for (int kk = 0; kk < kCPL; ++kk) d[kk] = col_sum(d[kk]);
+  for (int kk = kKmin; kk < kCPL; ++kk) d[kk] = col_sum(d[kk]);
 #pragma unroll
-  for (int kk = 0; kk < kCPL; ++kk) {
-    const float coef = col0 + 8 * kk > j ? sj * d[kk] : 0.f;
+  for (int kk = kKmin; kk < kCPL; ++kk) {
+    const float coef = col0 + kKK * kk > j ? sj * d[kk] : 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
       a[kk][4 * b + 0] = fmaf(-coef, u[b].x, a[kk][4 * b + 0]);
@@ -144,7 +155,7 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
   }
   if (pivot) {
     const int c = j + 1;
-    const int pk = (c % kCW) >> 3;
+    const int pk = SmallCfg<NP>::kCyclic ? (c / SmallCfg<NP>::kWarps) >> 3 : (c % kCW) >> 3;
 #pragma unroll
     for (int kk = 0; kk < kCPL; ++kk) {
       if (kk != pk) continue;
@@ -152,7 +163,7 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
       column_stats<NP, B0>(a[kk], c, rg, tail, alpha);
       tail = col_sum(tail);
       alpha = col_sum(alpha);
-      if (col0 + 8 * kk == c) {
+      if (col0 + kKK * kk == c) {
         mine[kk] = make_reflector(alpha, tail, c == n - 1);
         publish_u<NP, B0>(sm, a[kk], c, rg, mine[kk].v0);
         if (rg == 0) sm.S[c] = mine[kk].tau * mine[kk].inv_v0 * mine[kk].inv_v0;
@@ -166,13 +177,14 @@ template <int NP, int B0>
 __device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[kCPL][SmallCfg<NP>::kR],
                                            int j, int rg) {
   constexpr int kB = SmallCfg<NP>::kB;
+  constexpr int kKmin = SmallCfg<NP>::kCyclic ? 2 * B0 / SmallCfg<NP>::kWarps : 0;   // untouched blocks
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
   float d[kCPL];
 #pragma unroll
-  for (int kk = 0; kk < kCPL; ++kk) {
+  for (int kk = kKmin; kk < kCPL; ++kk) {
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -184,7 +196,7 @@ __device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[k
     d[kk] = (d0 + d1) + (d2 + d3);
   }
 #pragma unroll
-  for (int kk = 0; kk < kCPL; ++kk) {
+  for (int kk = kKmin; kk < kCPL; ++kk) {
     const float coef = sj * col_sum(d[kk]);
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -232,8 +244,10 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
   const int64_t b = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = lane >> 3, cl = lane & 7;
-  const int col0 = kCW * warp + cl;         // my columns: col0 + 8 * kk
-  const int wlast = kCW * warp + kCW - 1;   // last column of this warp
+  constexpr int kW = C::kWarps;
+  constexpr int kKK = C::kKKStep;
+  const int col0 = C::kCyclic ? warp + kW * cl : kCW * warp + cl;   // my columns: col0 + kKK * kk
+  const int wlast = C::kCyclic ? warp + kW * (kCW - 1) : kCW * warp + kCW - 1;   // my last column
   const size_t off = (size_t)b * n * n;
 
   float a[kCPL][R];
@@ -247,7 +261,7 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
     for (int kk = 0; kk < kCPL; ++kk)
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        const int row = row_of<NP>(rg, i), col = col0 + 8 * kk;
+        const int row = row_of<NP>(rg, i), col = col0 + kKK * kk;
         a[kk][i] = (row < n && col < n) ? __ldg(A + off + (size_t)row * n + col) : 0.f;
       }
     if (warp == 0) {   // reflector of column 0
@@ -263,14 +277,16 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
     }
     const int jlast = min(n - 1, wlast);
     for (int j = 0; j <= jlast; ++j) {
-      named_barrier(1, 32 * (C::kWarps - j / kCW));
-      const bool pivot = (j + 1 < n) && ((j + 1) / kCW == warp);
+      // the warps whose last column is >= j take part in step j
+      const int active = C::kCyclic ? kW - max(0, j - kW * (kCW - 1)) : kW - j / kCW;
+      named_barrier(1, 32 * active);
+      const bool pivot = (j + 1 < n) && (C::kCyclic ? (j + 1) % kW == warp : (j + 1) / kCW == warp);
       if (wlast > j) geqrf_step_dispatch<NP>(sm, a, j, n, rg, col0, pivot, mine);
     }
     // H: divide the sub-diagonal of each column by its v0, beta on the diagonal.
 #pragma unroll
     for (int kk = 0; kk < kCPL; ++kk) {
-      const int col = col0 + 8 * kk;
+      const int col = col0 + kKK * kk;
       if (col < n) {
 #pragma unroll
         for (int i = 0; i < R; ++i) {
@@ -286,7 +302,7 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
     // orgqr only: rebuild u_j = v_j (v0 := 1) and s_j = tau_j from (H, tau).
 #pragma unroll
     for (int kk = 0; kk < kCPL; ++kk) {
-      const int col = col0 + 8 * kk;
+      const int col = col0 + kKK * kk;
       if (col < n) {
 #pragma unroll
         for (int i = 0; i < R; ++i) {
@@ -308,12 +324,12 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
     for (int kk = 0; kk < kCPL; ++kk)
 #pragma unroll
       for (int i = 0; i < R; ++i)
-        a[kk][i] = (row_of<NP>(rg, i) == col0 + 8 * kk && col0 + 8 * kk < n) ? 1.f : 0.f;
+        a[kk][i] = (row_of<NP>(rg, i) == col0 + kKK * kk && col0 + kKK * kk < n) ? 1.f : 0.f;
     // Reflector j only touches columns >= j, so a warp starts at its last column.
     for (int j = min(n - 1, wlast); j >= 0; --j) orgqr_step_dispatch<NP>(sm, a, j, rg);
 #pragma unroll
     for (int kk = 0; kk < kCPL; ++kk) {
-      const int col = col0 + 8 * kk;
+      const int col = col0 + kKK * kk;
       if (col < n) {
 #pragma unroll
         for (int i = 0; i < R; ++i) {
