@@ -353,3 +353,51 @@ def test_cuda_graph_capture_and_replay(n):
         H, tau, Q = qrb().qr(B)
         torch.cuda.synchronize()
         assert torch.equal(H_g, H) and torch.equal(tau_g, tau) and torch.equal(Q_g, Q)
+
+
+def test_concurrent_calls_from_two_threads():
+    """Two host threads, each with its own stream and workspace, call the library at
+    the same time (small, blocked tensor-core and blocked SIMT sizes): every result
+    equals the sequential one bit for bit (the library's lazily built per-device state --
+    function attributes, the tensor-map encoder, device checks -- is thread-safe)."""
+    import threading
+    cases = [(64, 48), (6, 160), (4, 130)]
+    inputs = [torch.randn(b, n, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(n))
+              for b, n in cases]
+    ref = [qrb().qr(A) for A in inputs]
+    torch.cuda.synchronize()
+    results = [[None] * len(cases) for _ in range(2)]
+    errors = []
+
+    def worker(t):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for rep in range(3):
+                    for i, A in enumerate(inputs):
+                        results[t][i] = qrb().qr(A)
+            s.synchronize()
+        except Exception as e:   # surfaced below
+            errors.append(repr(e))
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(2)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors
+    for t in range(2):
+        for got, want in zip(results[t], ref):
+            assert all(torch.equal(g, w) for g, w in zip(got, want))
+
+
+@pytest.mark.parametrize("batch,n", [(9, 130), (40, 200)])
+def test_host_pipeline_simt_and_many_chunks(batch, n):
+    """Host pipeline on the SIMT blocked path (n % 4 != 0) and with 4 chunks of a
+    tensor-core size: same results as the device call."""
+    A_h = torch.randn(batch, n, n, generator=torch.Generator().manual_seed(n)).pin_memory()
+    H_h, t_h, Q_h = qrb().qr_host(A_h)
+    torch.cuda.current_stream().synchronize()
+    H, tau, Q = qrb().qr(A_h.cuda())
+    torch.cuda.synchronize()
+    assert torch.equal(H_h, H.cpu()) and torch.equal(t_h, tau.cpu()) and torch.equal(Q_h, Q.cpu())
