@@ -249,16 +249,17 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
 __global__ void __launch_bounds__(256)
 w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* __restrict__ w2, int64_t batch,
           int n, int c0, int nstrips, int nsplit, int trans_t) {
-  __shared__ float Ts[32][33];
-  __shared__ float Ws[kTN][33];
+  __shared__ __align__(16) float Tt[32][36];   // Tt[j][a] = op(T)[a][j]
+  __shared__ float Ws[kTN][33];                // Ws[i][j] = W^T[i][j]
   const int strip = blockIdx.x % nstrips;
   const int mat = blockIdx.x / nstrips;
   const int cs = c0 + strip * kTN;
   const float* T = Tg + (size_t)mat * 32 * 32;
   for (int idx = threadIdx.x; idx < 32 * 32; idx += blockDim.x) {
     const int r = idx >> 5, c = idx & 31;
-    const float t = __ldg(T + idx);
-    if (trans_t) Ts[c][r] = t; else Ts[r][c] = t;
+    const float t = __ldg(T + idx);   // T[r][c]
+    if (trans_t) Tt[r][c] = t;        // op(T) = T^T: op(T)[c][r] = T[r][c] -> Tt[r][c]
+    else Tt[c][r] = t;                // op(T) = T:   op(T)[r][c] = T[r][c] -> Tt[c][r]
   }
   for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
     const int i = idx >> 5, j = idx & 31;
@@ -268,13 +269,28 @@ w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* _
     Ws[i][j] = w;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
-    const int i = idx >> 5, a = idx & 31;   // strip column, reflector
-    if (cs + i >= n) continue;
-    float acc = 0.f;
+  // Thread: strip columns i0, i0 + 32 and reflectors a0..a0+3 (8 outputs, register tile).
+  const int i0 = threadIdx.x >> 3, a0 = (threadIdx.x & 7) * 4;
+  float acc[2][4] = {};
+#pragma unroll 8
+  for (int j = 0; j < 32; ++j) {
+    const float4 t = *reinterpret_cast<const float4*>(&Tt[j][a0]);
+    const float w0 = Ws[i0][j], w1 = Ws[i0 + 32][j];
+    acc[0][0] = fmaf(t.x, w0, acc[0][0]);
+    acc[0][1] = fmaf(t.y, w0, acc[0][1]);
+    acc[0][2] = fmaf(t.z, w0, acc[0][2]);
+    acc[0][3] = fmaf(t.w, w0, acc[0][3]);
+    acc[1][0] = fmaf(t.x, w1, acc[1][0]);
+    acc[1][1] = fmaf(t.y, w1, acc[1][1]);
+    acc[1][2] = fmaf(t.z, w1, acc[1][2]);
+    acc[1][3] = fmaf(t.w, w1, acc[1][3]);
+  }
 #pragma unroll
-    for (int j = 0; j < 32; ++j) acc = fmaf(Ts[a][j], Ws[i][j], acc);
-    w2[((size_t)mat * n + cs + i) * 32 + a] = acc;
+  for (int h = 0; h < 2; ++h) {
+    const int i = i0 + 32 * h;
+    if (cs + i < n)
+      *reinterpret_cast<float4*>(w2 + ((size_t)mat * n + cs + i) * 32 + a0) =
+          make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
   }
 }
 
