@@ -589,11 +589,13 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   const int m = n - k;
   const int nstrips = (n - c0 + kTN - 1) / kTN;
   const int ntiles = (m + kR3 - 1) / kR3;
-  // Row chunks for the W^T reduction: enough CTAs for ~2 waves at 3 per SM.
+  // Row chunks for the W^T reduction: up to ~8 waves of CTAs at 3 per SM, but never
+  // chunks under 512 rows (short chunks cost more in partial traffic and in the w2
+  // sum than they gain in balance; measured on b512_n256, b256_n512, b32_n2048).
   const int64_t units = (int64_t)nstrips * batch;
-  int nsplit = (int)((888 + units - 1) / units);
+  int nsplit = (int)((3552 + units - 1) / units);
   nsplit = nsplit < 1 ? 1 : (nsplit > kMaxSplit ? kMaxSplit : nsplit);
-  const int max_split = (m + 63) / 64;   // at least two 32-row stages per chunk
+  const int max_split = (m + 511) / 512;
   if (nsplit > max_split) nsplit = max_split < 1 ? 1 : max_split;
   int chunk = (m + nsplit - 1) / nsplit;
   chunk = (chunk + kR1 - 1) / kR1 * kR1;
