@@ -183,16 +183,12 @@ __device__ __forceinline__ float tf32_rn(float x) {
   return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
-// x = x0 + x1 + x2 with every piece representable in tf32: x0 = rn(x); r = x - x0 is
-// exact and keeps at most the 13 low significand bits of x; x1 = rn(r); x2 = r - x1 is
-// exact and has at most 2 significant bits, so it is a tf32 value as it stands.  With
-// the six products x0y0 + x0y1 + x1y0 + x0y2 + x1y1 + x2y0 a tf32 tensor-core product
-// carries about 24 bits, i.e. fp32 accuracy.
-__device__ __forceinline__ void split3_tf32(float x, float& x0, float& x1, float& x2) {
+// x = x0 + x1 with both pieces tf32 values: x0 = rn(x), x1 = rn(x - x0) (the difference
+// is exact).  |x - x0 - x1| <= 2^-22 |x|, and x0y0 + x0y1 + x1y0 (the 3xTF32 scheme) is
+// a product carrying about 22 bits; the dropped x1y1 is of the same weight.
+__device__ __forceinline__ void split2_tf32(float x, float& x0, float& x1) {
   x0 = tf32_rn(x);
-  const float r = x - x0;
-  x1 = tf32_rn(r);
-  x2 = r - x1;
+  x1 = tf32_rn(x - x0);
 }
 
 // Byte offset of logical (row, col) of fp32 tile whose rows are 128 bytes (32 floats)
