@@ -43,7 +43,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   __shared__ float cred_w[2][CL][32];
   __shared__ float crowj[2][32];
   __shared__ float Ts[32][33];                    // T factor (rank 0 only)
-  __shared__ float Gs[32][33];                    // strict upper part of V^T V (rank 0)
+  __shared__ float Gt[32][32];                    // Gt[j][c] = (V^T V)[c][j], c < j (rank 0)
   __shared__ float taus[32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -59,10 +59,6 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   for (int i = 0; i < RPT; ++i) {
     const int pr = row0 + 8 * i;
     a[i] = (pr < m && lane < b) ? __ldg(src + moff + (size_t)(k + pr) * n + k + lane) : 0.f;
-  }
-  if (warp == 0) {
-#pragma unroll 4
-    for (int c = 0; c < 32; ++c) Ts[lane][c] = 0.f;
   }
 
   // Reflectors are applied unscaled: u_j = (0.., v0, x_{j+1}, ..) and H_j = I - s u u^T
@@ -165,7 +161,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     // ---- record G[:j, j] = (V^T V)[c, j] and tau_j (warp 0 of rank 0) ----------
     // Lane c < j holds raw column c, so w = v0_j v0_c G[c][j].
     if (warp == 0 && rank == 0) {
-      if (lane < j) Gs[lane][j] = w * f.inv_v0 * my_inv;
+      if (lane < j) Gt[j][lane] = w * f.inv_v0 * my_inv;
       if (lane == 0) {
         taus[j] = f.tau;
         tau[(size_t)mat * n + k + j] = f.tau;
@@ -173,30 +169,31 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     }
   }
 
-  // ---- T factor after the column loop: lane i builds row i of T ------------------
-  // T[i][j] = -tau_j * sum_{c=i}^{j-1} T[i][c] G[c][j] (j > i), T[i][i] = tau_i: rows are
-  // independent, so the 32 recurrences run side by side instead of one per column step.
+  // ---- T factor after the column loop: lane i builds row i of T in registers -----
+  // T[i][j] = -tau_j * sum_{c<j} T[i][c] G[c][j] (j > i; T[i][c] = 0 for c < i),
+  // T[i][i] = tau_i: rows are independent, so the 32 recurrences run side by side; with
+  // the loops unrolled the row stays in registers and G[:, j] is a broadcast read.
   if (warp == 0 && rank == 0) {
     __syncwarp();
     const int i = lane;
+    float t[32];
+#pragma unroll
     for (int j = 0; j < 32; ++j) {
-      float t;
-      if (j < i || j >= b) {
-        t = 0.f;
-      } else if (j == i) {
-        t = taus[j];
-      } else {
-        float s0 = 0.f, s1 = 0.f;
-        int c = i;
-        for (; c + 1 < j; c += 2) {
-          s0 = fmaf(Ts[i][c], Gs[c][j], s0);
-          s1 = fmaf(Ts[i][c + 1], Gs[c + 1][j], s1);
-        }
-        if (c < j) s0 = fmaf(Ts[i][c], Gs[c][j], s0);
-        t = -taus[j] * (s0 + s1);
+      float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+      for (int c = 0; c + 3 < j; c += 4) {
+        s0 = fmaf(t[c], Gt[j][c], s0);
+        s1 = fmaf(t[c + 1], Gt[j][c + 1], s1);
+        s2 = fmaf(t[c + 2], Gt[j][c + 2], s2);
+        s3 = fmaf(t[c + 3], Gt[j][c + 3], s3);
       }
-      Ts[i][j] = t;
+#pragma unroll
+      for (int c = j & ~3; c < j; ++c) s0 = fmaf(t[c], Gt[j][c], s0);
+      const float v = -taus[j] * ((s0 + s1) + (s2 + s3));
+      t[j] = (j < i || j >= b) ? 0.f : (j == i ? taus[j] : v);
     }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) Ts[i][j] = t[j];
   }
 
   // ---- write back panel (v = raw / v0 below, beta on the diagonal) and T ------
