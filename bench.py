@@ -53,15 +53,33 @@ def bytes_per_matrix(n: int) -> int:
     return 12 * n * n + 4 * n
 
 
-def kernel_launches(n: int) -> int:
+def _tc_update_launches(batch: int, n: int, k: int, c0: int) -> int:
+    """Launches of one tensor-core update (launch_split in csrc/qrb_apply_tc.cu): wpart, the
+    w2 sum only when the W^T reduction is split over row chunks, and the update."""
+    m = n - k
+    units = -(-(n - c0) // 64) * batch
+    nsplit = min(max(-(-3552 // units), 1), 8)
+    nsplit = min(nsplit, max(1, -(-m // 512)))
+    chunk = -(-(-(-m // nsplit)) // 32) * 32
+    nsplit = -(-m // chunk)
+    return 2 if nsplit == 1 else 3
+
+
+def kernel_launches(n: int, batch: int = 1) -> int:
     """libqrb200 kernels one fused QR enqueues (see csrc/qrb_api.cu dispatch)."""
     if n <= 64:
         return 1
     np_ = (n + 31) // 32
-    applies = (np_ - 1) + np_         # trailing updates + orgqr blocks
-    # tensor-core path (n % 4 == 0): W^T partials, W2, update per block
-    per_apply = 3 if n % 4 == 0 else 1
-    return np_ + applies * per_apply
+    if n % 4 != 0:                    # SIMT update: one launch per block
+        return np_ + (np_ - 1) + np_
+    total = np_
+    for p in range(np_):              # geqrf trailing updates
+        k = 32 * p
+        if k + 32 < n:
+            total += _tc_update_launches(batch, n, k, k + 32)
+    for p in range(np_):              # orgqr blocks
+        total += _tc_update_launches(batch, n, 32 * p, 32 * p)
+    return total
 
 
 def dominant_kernel(n: int) -> str:
@@ -335,7 +353,7 @@ def run_ours(args) -> dict | None:
                    "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed between steps (256 MiB write)",
                    "op": "geqrf + orgqr (qrb_qr_f32)"},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": kernel_launches(n) * args.steps,
+        "gpu_launches": kernel_launches(n, batch) * args.steps,
         "clocks": clocks.summary(),
     }
 

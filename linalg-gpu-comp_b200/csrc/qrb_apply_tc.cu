@@ -99,14 +99,16 @@ constexpr uint32_t kWBox = kTN * 128;   // W2 piece box: 64 strip columns x 32 f
 
 // ---- (A) W^T partial over one row chunk: part[split][mat][strip][64][32] -------------
 // Three CTAs per SM: two 24 KB stages.  V arrives raw from H (masked to the unit lower
-// trapezoid here) and is split with C.
+// trapezoid here) and is split with C.  With a single row chunk (nsplit == 1) the CTA
+// holds the whole W^T of its strip and finishes W2 = op(T) W itself (the work of
+// w2_kernel, same arithmetic order), so the update needs no second launch.
 constexpr uint32_t kSmemA = 2 * kStage1 + 64 + 1024;
 
 template <bool IDENT>
 __global__ void __launch_bounds__(kThreads, 3)
 wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constant__ CUtensorMap map_hv32,
-             float* __restrict__ part, int64_t batch, int n, int k, int b, int c0, int nstrips, int chunk,
-             int nsplit) {
+             float* __restrict__ part, const float* __restrict__ Tg, float* __restrict__ w2, int64_t batch,
+             int n, int k, int b, int c0, int nstrips, int chunk, int nsplit, int trans_t) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
@@ -124,6 +126,12 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   const int r1 = min(n, r0 + chunk);
   const int nst = (r1 - r0 + kR1 - 1) / kR1;   // chunk % 32 == 0: stages never cross chunks
   const int kb = k + b;
+  // T of the panel, fetched early for the direct W2 path: thread holds T[tid / 32 + 4e][tid % 32].
+  float treg[8];
+  if (nsplit == 1) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) treg[e] = __ldg(Tg + (size_t)mat * 32 * 32 + tid + 128 * e);
+  }
 
   if (tid == 0) {
     mbar_init(&tma1[0], 1);
@@ -230,7 +238,46 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   }
   gather_stage(nst - 1);
   // M = 64 accumulator: lanes 0-15 of warp w hold W^T rows 16w + lane.
-  if (lane < 16) {
+  if (nsplit == 1) {
+    // Every MMA has completed (gathered), so the stage buffers are free.
+    __syncthreads();
+    float(*Ws)[33] = reinterpret_cast<float(*)[33]>(sm);                   // Ws[i][j] = W^T[i][j]
+    float(*Tt)[36] = reinterpret_cast<float(*)[36]>(sm + kTN * 33 * 4);   // Tt[j][a] = op(T)[a][j]
+    if (lane < 16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) Ws[16 * warp + lane][j] = wacc[j];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int r = (tid >> 5) + 4 * e, c = tid & 31;   // treg[e] = T[r][c]
+      if (trans_t) Tt[r][c] = treg[e];
+      else Tt[c][r] = treg[e];
+    }
+    __syncthreads();
+    // Thread: strip columns i0, i0 + 32 and reflectors a0..a0+7.
+    const int i0 = tid >> 2, a0 = (tid & 3) * 8;
+    float acc[2][8] = {};
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) {
+      const float4 ta = *reinterpret_cast<const float4*>(&Tt[j][a0]);
+      const float4 tb = *reinterpret_cast<const float4*>(&Tt[j][a0 + 4]);
+      const float tv[8] = {ta.x, ta.y, ta.z, ta.w, tb.x, tb.y, tb.z, tb.w};
+      const float wv[2] = {Ws[i0][j], Ws[i0 + 32][j]};
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[h][e] = fmaf(tv[e], wv[h], acc[h][e]);
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = i0 + 32 * h;
+      if (cs + i < n) {
+        float4* dst = reinterpret_cast<float4*>(w2 + ((size_t)mat * n + cs + i) * 32 + a0);
+        dst[0] = make_float4(acc[h][0], acc[h][1], acc[h][2], acc[h][3]);
+        dst[1] = make_float4(acc[h][4], acc[h][5], acc[h][6], acc[h][7]);
+      }
+    }
+  } else if (lane < 16) {
     const int i = 16 * warp + lane;
     float4* dst = reinterpret_cast<float4*>(
         part + ((((size_t)split * batch + mat) * nstrips + strip) * kTN + i) * 32);
@@ -602,13 +649,15 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   int chunk = (m + nsplit - 1) / nsplit;
   chunk = (chunk + kR1 - 1) / kR1 * kR1;
   nsplit = (m + chunk - 1) / chunk;
-  wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(s32, v32, part, batch, n, k, b, c0,
-                                                                            nstrips, chunk, nsplit);
+  wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(
+      s32, v32, part, T, w2, batch, n, k, b, c0, nstrips, chunk, nsplit, trans_t);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  w2_kernel<<<(unsigned)units, 256, 0, st>>>(part, T, w2, batch, n, c0, nstrips, nsplit, trans_t);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  if (nsplit > 1) {
+    w2_kernel<<<(unsigned)units, 256, 0, st>>>(part, T, w2, batch, n, c0, nstrips, nsplit, trans_t);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   // Persistent update: at least four items per SM so the last round is short; strip
   // groups (each reloading V) only when there are too few row tiles for that.
   const int64_t tiles = batch * ntiles;

@@ -53,5 +53,9 @@ def test_bench_accounting():
     assert bench.flops_per_matrix(3) == pytest.approx(72.0)
     assert bench.kernel_launches(64) == 1
     # n = 256: 8 panels, 7 trailing updates, 8 orgqr blocks
-    assert bench.kernel_launches(256) == 8 + (7 + 8) * 3          # panels + 3 launches per tensor-core update
+    # one row chunk for m <= 512: wpart (with W2) + update per tensor-core update
+    assert bench.kernel_launches(256) == 8 + (7 + 8) * 2
+    assert bench.kernel_launches(256, 4096) == 8 + (7 + 8) * 2
+    # n = 2048 at batch 32: tall blocks split the W^T reduction and add the w2 sum
+    assert 64 + 127 * 2 < bench.kernel_launches(2048, 32) <= 64 + 127 * 3
     assert bench.kernel_launches(258) == 9 + (8 + 9)              # n % 4 != 0: one SIMT launch per update
