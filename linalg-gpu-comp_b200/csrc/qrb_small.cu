@@ -6,10 +6,11 @@
 // step, and adds the Q formation its checker does with householder_product
 // (reference_repo/reference.py:144).
 //
-// Layout.  NP (32 or 64) is n rounded up.  Four lanes share a column: lane =
-// 8*rg + cl (rg in 0..3) of warp w owns two columns -- 16w + cl and 16w + 8 + cl for
-// NP = 64, w + 2cl and w + 2cl + 16 for NP = 32 (see SmallCfg::kCyclic) -- and the
-// rows {rg + 4i}, all in registers, so the CTA has NP/16 warps (small register
+// n <= 32 takes tiny_qr_kernel (one warp per matrix, at the end of this file).
+//
+// Layout (32 < n <= 64).  NP = 64 is n rounded up.  Four lanes share a column: lane =
+// 8*rg + cl (rg in 0..3) of warp w owns two columns -- 16w + cl and 16w + 8 + cl -- and
+// the rows {rg + 4i}, all in registers, so the CTA has NP/16 warps (small register
 // footprint per matrix: more matrices in flight per SM).  A column reduction over rows is a
 // register sum plus two xor shuffles (8, 16).
 //
@@ -41,13 +42,9 @@ struct SmallCfg {
   static constexpr int kR = NP / kRG;    // rows per lane
   static constexpr int kB = kR / 4;      // float4 blocks per lane (4*kRG matrix rows each)
   static constexpr int kBlockRows = 4 * kRG;
-  // Column ownership.  Cyclic (warp w owns columns w, w + kWarps, ..): every warp keeps
-  // work to the last step and each step's update is spread over all warps -- shorter
-  // steps, more issued instructions; measured faster for n <= 32 (latency-bound, few
-  // matrices) and slower for n = 64.  Blocked (warp w owns 16 consecutive columns):
-  // warps retire as the factorisation passes them.
-  static constexpr bool kCyclic = NP == 32;
-  static constexpr int kKKStep = kCyclic ? 8 * kWarps : 8;      // between a lane's kk columns
+  // Column ownership is blocked (warp w owns 16 consecutive columns), so warps retire
+  // as the factorisation passes them.
+  static constexpr int kKKStep = 8;      // between a lane's kk columns
 };
 
 __device__ __forceinline__ void named_barrier(int id, int count) {
@@ -121,15 +118,13 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
                                            int n, int rg, int col0, bool pivot, Reflector (&mine)[kCPL]) {
   constexpr int kB = SmallCfg<NP>::kB;
   constexpr int kKK = SmallCfg<NP>::kKKStep;
-  // cyclic ownership: column blocks kk < kKmin lie left of row block B0 (all done)
-  constexpr int kKmin = SmallCfg<NP>::kCyclic ? 2 * B0 / SmallCfg<NP>::kWarps : 0;
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
   float d[kCPL];
 #pragma unroll
-  for (int kk = kKmin; kk < kCPL; ++kk) {
+  for (int kk = 0; kk < kCPL; ++kk) {
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -141,9 +136,9 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
     d[kk] = (d0 + d1) + (d2 + d3);
   }
 #pragma unroll
-  for (int kk = kKmin; kk < kCPL; ++kk) d[kk] = col_sum(d[kk]);
+  for (int kk = 0; kk < kCPL; ++kk) d[kk] = col_sum(d[kk]);
 #pragma unroll
-  for (int kk = kKmin; kk < kCPL; ++kk) {
+  for (int kk = 0; kk < kCPL; ++kk) {
     const float coef = col0 + kKK * kk > j ? sj * d[kk] : 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -155,7 +150,7 @@ __device__ __forceinline__ void geqrf_step(SmallSmem<NP>& sm, float (&a)[kCPL][S
   }
   if (pivot) {
     const int c = j + 1;
-    const int pk = SmallCfg<NP>::kCyclic ? (c / SmallCfg<NP>::kWarps) >> 3 : (c % kCW) >> 3;
+    const int pk = (c % kCW) >> 3;
 #pragma unroll
     for (int kk = 0; kk < kCPL; ++kk) {
       if (kk != pk) continue;
@@ -177,14 +172,13 @@ template <int NP, int B0>
 __device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[kCPL][SmallCfg<NP>::kR],
                                            int j, int rg) {
   constexpr int kB = SmallCfg<NP>::kB;
-  constexpr int kKmin = SmallCfg<NP>::kCyclic ? 2 * B0 / SmallCfg<NP>::kWarps : 0;   // untouched blocks
   float4 u[kB];
 #pragma unroll
   for (int b = B0; b < kB; ++b) u[b] = sm.U[j][rg][b];
   const float sj = sm.S[j];
   float d[kCPL];
 #pragma unroll
-  for (int kk = kKmin; kk < kCPL; ++kk) {
+  for (int kk = 0; kk < kCPL; ++kk) {
     float d0 = 0.f, d1 = 0.f, d2 = 0.f, d3 = 0.f;
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -196,7 +190,7 @@ __device__ __forceinline__ void orgqr_step(const SmallSmem<NP>& sm, float (&q)[k
     d[kk] = (d0 + d1) + (d2 + d3);
   }
 #pragma unroll
-  for (int kk = kKmin; kk < kCPL; ++kk) {
+  for (int kk = 0; kk < kCPL; ++kk) {
     const float coef = sj * col_sum(d[kk]);
 #pragma unroll
     for (int b = B0; b < kB; ++b) {
@@ -246,8 +240,8 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
   const int rg = lane >> 3, cl = lane & 7;
   constexpr int kW = C::kWarps;
   constexpr int kKK = C::kKKStep;
-  const int col0 = C::kCyclic ? warp + kW * cl : kCW * warp + cl;   // my columns: col0 + kKK * kk
-  const int wlast = C::kCyclic ? warp + kW * (kCW - 1) : kCW * warp + kCW - 1;   // my last column
+  const int col0 = kCW * warp + cl;          // my columns: col0 + kKK * kk
+  const int wlast = kCW * warp + kCW - 1;    // my last column
   const size_t off = (size_t)b * n * n;
 
   float a[kCPL][R];
@@ -278,9 +272,9 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
     const int jlast = min(n - 1, wlast);
     for (int j = 0; j <= jlast; ++j) {
       // the warps whose last column is >= j take part in step j
-      const int active = C::kCyclic ? kW - max(0, j - kW * (kCW - 1)) : kW - j / kCW;
+      const int active = kW - j / kCW;
       named_barrier(1, 32 * active);
-      const bool pivot = (j + 1 < n) && (C::kCyclic ? (j + 1) % kW == warp : (j + 1) / kCW == warp);
+      const bool pivot = (j + 1 < n) && (j + 1) / kCW == warp;
       if (wlast > j) geqrf_step_dispatch<NP>(sm, a, j, n, rg, col0, pivot, mine);
     }
     // H: divide the sub-diagonal of each column by its v0, beta on the diagonal.
@@ -341,13 +335,110 @@ small_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __res
   }
 }
 
+// ---- n <= 32: one warp per matrix, lane c owns column c (all 32 rows in registers) ----
+// Every dot product over rows stays inside a lane, so a step is one broadcast of column
+// j (a shuffle per row below the pivot, every lane forming the same ||x||^2 in the same
+// order) and lane-local FMAs -- no barrier and no shared memory.  The steps are fully
+// unrolled, so row predicates are resolved at compile time.  geqrf follows
+// submissions/v1.py:9-38 (via make_reflector); orgqr is the same backward accumulation as
+// the n <= 64 kernel.
+constexpr int kTinyWarps = 4;
+
+__global__ void __launch_bounds__(kTinyWarps * 32)
+tiny_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __restrict__ tau,
+               float* __restrict__ Q, int64_t batch, int n, int mode) {
+  constexpr unsigned kFull = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  const int64_t mat = (int64_t)blockIdx.x * kTinyWarps + (threadIdx.x >> 5);
+  if (mat >= batch) return;   // whole warp
+  const size_t moff = (size_t)mat * n * n;
+  const bool col = lane < n;
+  float a[32];
+  float my_tau = 0.f;
+  if (mode & 1) {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) a[r] = (r < n && col) ? __ldg(A + moff + (size_t)r * n + lane) : 0.f;
+    // Reflectors are applied unscaled (u = (v0, x_{j+1}, ..), H_j = I - (tau / v0^2) u u^T);
+    // lane j keeps its raw column and scales it once at the end.
+    float my_inv = 1.f, my_beta = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (j < n) {
+        const float alpha = __shfl_sync(kFull, a[j], j);
+        float x[32];
+        float t0 = 0.f, t1 = 0.f, d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int r = j + 1; r < 32; ++r) {
+          x[r] = __shfl_sync(kFull, a[r], j);
+          if ((r - j) & 1) {
+            t0 = fmaf(x[r], x[r], t0);
+            d0 = fmaf(x[r], a[r], d0);
+          } else {
+            t1 = fmaf(x[r], x[r], t1);
+            d1 = fmaf(x[r], a[r], d1);
+          }
+        }
+        const Reflector f = make_reflector(alpha, t0 + t1, j == n - 1);
+        const float w = fmaf(f.v0, a[j], d0 + d1);   // u^T a_c
+        const float coef = lane > j ? f.tau * f.inv_v0 * f.inv_v0 * w : 0.f;
+        a[j] = fmaf(-coef, f.v0, a[j]);
+#pragma unroll
+        for (int r = j + 1; r < 32; ++r) a[r] = fmaf(-coef, x[r], a[r]);
+        if (lane == j) {
+          my_inv = f.inv_v0;
+          my_beta = f.beta;
+          my_tau = f.tau;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      a[r] = r > lane ? a[r] * my_inv : (r == lane ? my_beta : a[r]);
+      if (r < n && col) H[moff + (size_t)r * n + lane] = a[r];
+    }
+    if (col) tau[(size_t)mat * n + lane] = my_tau;
+  } else {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) a[r] = (r < n && col) ? __ldg(H + moff + (size_t)r * n + lane) : 0.f;
+    if (col) my_tau = __ldg(tau + (size_t)mat * n + lane);
+  }
+  if (mode & 2) {
+    // Q = H_0 H_1 .. H_{n-1} I, accumulated backwards; lane c owns column c of Q.
+    float q[32];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) q[r] = r == lane ? 1.f : 0.f;
+#pragma unroll
+    for (int j = 31; j >= 0; --j) {
+      if (j < n) {
+        const float tj = __shfl_sync(kFull, my_tau, j);
+        float v[32];
+        float w0 = q[j], w1 = 0.f;   // v_j = 1
+#pragma unroll
+        for (int r = j + 1; r < 32; ++r) {
+          v[r] = __shfl_sync(kFull, a[r], j);
+          if ((r - j) & 1) w1 = fmaf(v[r], q[r], w1);
+          else w0 = fmaf(v[r], q[r], w0);
+        }
+        const float c = tj * (w0 + w1);
+        q[j] -= c;
+#pragma unroll
+        for (int r = j + 1; r < 32; ++r) q[r] = fmaf(-c, v[r], q[r]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 32; ++r)
+      if (r < n && col) Q[moff + (size_t)r * n + lane] = q[r];
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_small(const float* A, float* H, float* tau, float* Q,
                          int64_t batch, int n, int mode, cudaStream_t s) {
   if (batch == 0) return cudaSuccess;
   if (n <= 32) {
-    small_qr_kernel<32><<<(unsigned)batch, SmallCfg<32>::kThreads, 0, s>>>(A, H, tau, Q, n, mode);
+    const unsigned grid = (unsigned)((batch + kTinyWarps - 1) / kTinyWarps);
+    tiny_qr_kernel<<<grid, kTinyWarps * 32, 0, s>>>(A, H, tau, Q, batch, n, mode);
   } else {
     small_qr_kernel<64><<<(unsigned)batch, SmallCfg<64>::kThreads, 0, s>>>(A, H, tau, Q, n, mode);
   }

@@ -21,8 +21,32 @@ from . import _lib
 _QUEUE_ATTR = "cuda_" + "str" + "eam"   # handle attribute of torch.cuda.Stream
 
 
+_raw_queue = getattr(torch._C, "_cuda_getCurrentRawStream", None)   # int handle, no Stream object
+
+
 def _queue_handle(device: torch.device) -> int:
+    if _raw_queue is not None and device.index is not None:
+        return _raw_queue(device.index)
     return getattr(torch.cuda.current_stream(device), _QUEUE_ATTR)
+
+
+class _OnDevice:
+    """``torch.cuda.device(dev)`` that costs nothing when ``dev`` is already current
+    (the common case: one process per GPU)."""
+
+    __slots__ = ("ctx",)
+
+    def __init__(self, device: torch.device):
+        idx = device.index
+        self.ctx = None if idx is None or idx == torch.cuda.current_device() else torch.cuda.device(device)
+
+    def __enter__(self):
+        if self.ctx is not None:
+            self.ctx.__enter__()
+
+    def __exit__(self, *exc):
+        if self.ctx is not None:
+            self.ctx.__exit__(*exc)
 
 
 def _check_batch(x: torch.Tensor, name: str) -> torch.Tensor:
@@ -32,13 +56,18 @@ def _check_batch(x: torch.Tensor, name: str) -> torch.Tensor:
         raise TypeError(f"{name} must be float32 (got {x.dtype})")
     if x.dim() != 3 or x.shape[-1] != x.shape[-2]:
         raise ValueError(f"{name} must have shape (batch, n, n) (got {tuple(x.shape)})")
-    if x.device.type != "cuda":
+    if not x.is_cuda:
         raise ValueError(f"{name} must be a CUDA tensor (got {x.device}); libqrb200 has no CPU path")
     return x.contiguous()
 
 
+_ws_sizes: dict[tuple[int, int], int] = {}
+
+
 def _workspace(batch: int, n: int, device: torch.device) -> tuple[int, int, torch.Tensor | None]:
-    nbytes = int(_lib.lib().qrb_workspace_size(batch, n))
+    nbytes = _ws_sizes.get((batch, n))
+    if nbytes is None:
+        nbytes = _ws_sizes[(batch, n)] = int(_lib.lib().qrb_workspace_size(batch, n))
     if nbytes == 0:
         return 0, 0, None
     ws = torch.empty(nbytes, dtype=torch.uint8, device=device)
@@ -54,7 +83,7 @@ def geqrf(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor] | None = None)
         tau = torch.empty((batch, n), dtype=A.dtype, device=A.device)
     else:
         H, tau = out
-    with torch.cuda.device(A.device):
+    with _OnDevice(A.device):
         wp, wb, _ws = _workspace(batch, n, A.device)
         _lib.check(_lib.lib().qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), batch, n,
                                             wp, wb, _queue_handle(A.device)))
@@ -69,7 +98,7 @@ def orgqr(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
         raise ValueError(f"tau must be float32 ({batch}, {n}) on {H.device}")
     tau = tau.contiguous()
     Q = torch.empty_like(H)
-    with torch.cuda.device(H.device):
+    with _OnDevice(H.device):
         wp, wb, _ws = _workspace(batch, n, H.device)
         _lib.check(_lib.lib().qrb_orgqr_f32(H.data_ptr(), tau.data_ptr(), Q.data_ptr(), batch, n,
                                             wp, wb, _queue_handle(H.device)))
@@ -86,7 +115,7 @@ def qr(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | N
         Q = torch.empty_like(A)
     else:
         H, tau, Q = out
-    with torch.cuda.device(A.device):
+    with _OnDevice(A.device):
         wp, wb, _ws = _workspace(batch, n, A.device)
         _lib.check(_lib.lib().qrb_qr_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), Q.data_ptr(),
                                          batch, n, wp, wb, _queue_handle(A.device)))
