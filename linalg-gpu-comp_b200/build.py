@@ -68,5 +68,45 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     return OUT
 
 
+ENTRY_SRC = PKG / "qr_b200" / "_entry.cpp"
+
+
+def _entry_out() -> Path:
+    import sysconfig
+    return PKG / "qr_b200" / ("_entry" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_entry(force: bool = False, verbose: bool = False) -> Path:
+    """Compile qr_b200/_entry.cpp (the torch-facing call path, pybind11) against the
+    in-tree libqrb200.so, with rpath $ORIGIN so the pair travels together."""
+    import sysconfig
+
+    import torch
+    import torch.utils.cpp_extension as ce
+
+    out = _entry_out()
+    deps = [ENTRY_SRC, OUT, INCLUDE / "qrb200.h", Path(__file__)]
+    if not force and out.exists() and all(d.stat().st_mtime <= out.stat().st_mtime for d in deps):
+        return out
+    cxx = shutil.which("g++") or "c++"
+    inc = [f"-I{p}" for p in ce.include_paths()] + [f"-I{sysconfig.get_paths()['include']}", f"-I{INCLUDE}",
+                                                   "-I/usr/local/cuda/include"]
+    libdirs = ce.library_paths()
+    cmd = [cxx, "-O2", "-shared", "-fPIC", "-std=c++17", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_entry", "-DTORCH_API_INCLUDE_EXTENSION_H", *inc, str(ENTRY_SRC),
+           "-o", str(out.with_suffix(".tmp")), *[f"-L{d}" for d in libdirs], f"-L{OUT.parent}",
+           "-lqrb200", "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_python",
+           "-Wl,-rpath,$ORIGIN", *[f"-Wl,-rpath,{d}" for d in libdirs]]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed on {ENTRY_SRC.name}:\n{r.stdout}\n{r.stderr}")
+    os.replace(out.with_suffix(".tmp"), out)
+    return out
+
+
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose=True))
+    print(build_entry(force="--force" in sys.argv, verbose=True))

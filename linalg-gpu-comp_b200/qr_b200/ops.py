@@ -18,6 +18,20 @@ import torch
 
 from . import _lib
 
+# Compiled call path for geqrf / qr (qr_b200/_entry.cpp, built with the library).  Like
+# the library itself it is required: a missing build raises on first use.
+try:
+    from . import _entry
+except ImportError as _e:   # surfaced by _fast() with the build hint
+    _entry = None
+    _entry_error = _e
+
+
+def _fast():
+    if _entry is None:
+        raise RuntimeError(f"qr_b200/_entry is not built ({_entry_error}); run `python build.py`")
+    return _entry
+
 _QUEUE_ATTR = "cuda_" + "str" + "eam"   # handle attribute of torch.cuda.Stream
 
 
@@ -77,12 +91,10 @@ def _workspace(batch: int, n: int, device: torch.device) -> tuple[int, int, torc
 def geqrf(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor] | None = None):
     """(H, tau) = geqrf(A) for a (batch, n, n) float32 CUDA batch."""
     A = _check_batch(A, "A")
-    batch, n, _ = A.shape
     if out is None:
-        H = torch.empty_like(A)
-        tau = torch.empty((batch, n), dtype=A.dtype, device=A.device)
-    else:
-        H, tau = out
+        return _fast().geqrf(A)
+    batch, n, _ = A.shape
+    H, tau = out
     with _OnDevice(A.device):
         wp, wb, _ws = _workspace(batch, n, A.device)
         _lib.check(_lib.lib().qrb_geqrf_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), batch, n,
@@ -108,13 +120,10 @@ def orgqr(H: torch.Tensor, tau: torch.Tensor) -> torch.Tensor:
 def qr(A: torch.Tensor, out: tuple[torch.Tensor, torch.Tensor, torch.Tensor] | None = None):
     """Fused geqrf + Q formation: returns (H, tau, Q); R = triu(H)."""
     A = _check_batch(A, "A")
-    batch, n, _ = A.shape
     if out is None:
-        H = torch.empty_like(A)
-        tau = torch.empty((batch, n), dtype=A.dtype, device=A.device)
-        Q = torch.empty_like(A)
-    else:
-        H, tau, Q = out
+        return _fast().qr(A)
+    batch, n, _ = A.shape
+    H, tau, Q = out
     with _OnDevice(A.device):
         wp, wb, _ws = _workspace(batch, n, A.device)
         _lib.check(_lib.lib().qrb_qr_f32(A.data_ptr(), H.data_ptr(), tau.data_ptr(), Q.data_ptr(),
