@@ -95,6 +95,14 @@ def test_empty_batch_is_a_no_op(lib):
     assert lib.qrb_qr_f32(FAKE, FAKE, FAKE, FAKE + 256, 0, 300, None, 0, None) == 0
 
 
+def test_compiled_call_path_loads():
+    """The compiled torch call path (qr_b200/_entry.cpp) is built next to the library,
+    links it, and exposes the two hot calls (no GPU needed to load it)."""
+    from qr_b200 import ops
+    assert ops._entry is not None, "qr_b200/_entry is not built"
+    assert callable(ops._fast().geqrf) and callable(ops._fast().qr)
+
+
 def test_python_ops_reject_cpu_and_wrong_dtype():
     import torch
     from qr_b200 import custom_kernel, form_q

@@ -137,7 +137,7 @@ def test_sizes_qr(n):
     assert (Q2 - Q).abs().max().item() <= 1e-5
 
 
-@pytest.mark.parametrize("n", [33, 64, 96, 130, 300])
+@pytest.mark.parametrize("n", [5, 17, 32, 33, 64, 96, 130, 300])
 def test_matches_oracle_at_small_sizes(n):
     A_np = np.random.default_rng(n).standard_normal((2, n, n)).astype(np.float32)
     H, tau, Q = qrb().qr(torch.from_numpy(A_np).cuda())
@@ -401,3 +401,31 @@ def test_host_pipeline_simt_and_many_chunks(batch, n):
     H, tau, Q = qrb().qr(A_h.cuda())
     torch.cuda.synchronize()
     assert torch.equal(H_h, H.cpu()) and torch.equal(t_h, tau.cpu()) and torch.equal(Q_h, Q.cpu())
+
+
+@pytest.mark.parametrize("batch,n", [(7, 17), (64, 64), (5, 200), (3, 300)])
+def test_compiled_call_path_matches_ctypes(batch, n):
+    """geqrf / qr through the compiled entry (qr_b200/_entry.cpp, the default) and through
+    the ctypes binding (the out= form) launch the same kernels: identical results."""
+    A = torch.randn(batch, n, n, device="cuda", generator=torch.Generator(device="cuda").manual_seed(n))
+    H1, t1 = qrb().geqrf(A)
+    H2, t2 = torch.empty_like(A), torch.empty(batch, n, device="cuda")
+    qrb().geqrf(A, out=(H2, t2))
+    assert torch.equal(H1, H2) and torch.equal(t1, t2)
+    Hq, tq, Q1 = qrb().qr(A)
+    out = (torch.empty_like(A), torch.empty(batch, n, device="cuda"), torch.empty_like(A))
+    qrb().qr(A, out=out)
+    assert torch.equal(Hq, out[0]) and torch.equal(tq, out[1]) and torch.equal(Q1, out[2])
+
+
+def test_compiled_call_path_follows_current_stream_and_device():
+    """Work goes to torch's current stream: results are ready after that stream syncs."""
+    A = torch.randn(16, 96, 96, device="cuda")
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        H, tau = qrb().custom_kernel(A)
+    s.synchronize()
+    H2, t2 = qrb().custom_kernel(A)
+    torch.cuda.synchronize()
+    assert torch.equal(H, H2) and torch.equal(tau, t2)
