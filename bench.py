@@ -53,33 +53,11 @@ def bytes_per_matrix(n: int) -> int:
     return 12 * n * n + 4 * n
 
 
-def _tc_update_launches(batch: int, n: int, k: int, c0: int) -> int:
-    """Launches of one tensor-core update (launch_split in csrc/qrb_apply_tc.cu): wpart, the
-    w2 sum only when the W^T reduction is split over row chunks, and the update."""
-    m = n - k
-    units = -(-(n - c0) // 64) * batch
-    nsplit = min(max(-(-3552 // units), 1), 8)
-    nsplit = min(nsplit, max(1, -(-m // 512)))
-    chunk = -(-(-(-m // nsplit)) // 32) * 32
-    nsplit = -(-m // chunk)
-    return 2 if nsplit == 1 else 3
-
-
 def kernel_launches(n: int, batch: int = 1) -> int:
-    """libqrb200 kernels one fused QR enqueues (see csrc/qrb_api.cu dispatch)."""
-    if n <= 64:
-        return 1
-    np_ = (n + 31) // 32
-    if n % 4 != 0:                    # SIMT update: one launch per block
-        return np_ + (np_ - 1) + np_
-    total = np_
-    for p in range(np_):              # geqrf trailing updates
-        k = 32 * p
-        if k + 32 < n:
-            total += _tc_update_launches(batch, n, k, k + 32)
-    for p in range(np_):              # orgqr blocks
-        total += _tc_update_launches(batch, n, 32 * p, 32 * p)
-    return total
+    """libqrb200 kernels one fused QR enqueues, as the library itself counts them
+    (qrb_kernel_launches mirrors its dispatch in csrc/qrb_api.cu)."""
+    import qr_b200
+    return int(qr_b200.lib().qrb_kernel_launches(batch, n, 1))
 
 
 def dominant_kernel(n: int) -> str:

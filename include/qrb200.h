@@ -89,6 +89,13 @@ QRB_API int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t b
  * (its kernels have no device-side waits). */
 QRB_API int qrb_device_error(void);
 
+/* Number of kernels one qrb_qr_f32 (with_q != 0) or qrb_geqrf_f32 (with_q == 0) call
+ * enqueues for (batch, n): 1 for n <= 64, otherwise one panel per 32 columns plus two or
+ * three per block update (three when the W^T reduction is split over row chunks; one on
+ * the SIMT path, n % 4 != 0).  0 for an empty batch or an unsupported n.  For graph
+ * builders and launch accounting; no counterpart in the reference. */
+QRB_API int64_t qrb_kernel_launches(int64_t batch, int n, int with_q);
+
 /* (H, tau) = geqrf(A) without any caller workspace, for callers that cannot
  * allocate device memory (a plugin host that passes only raw input/output pointers,
  * or a path that must not enter the allocator).  No counterpart in the reference.

@@ -149,6 +149,22 @@ int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
   return Q != nullptr ? blocked_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
 }
 
+// Kernels run_qr enqueues (it mirrors that dispatch).
+int64_t count_launches(int64_t batch, int n, bool with_q) {
+  if (n <= qrb::kSmallMaxN) return 1;
+  const int np = n_panels(n);
+  auto update = [&](int k, int c0) -> int64_t {
+    return n % 4 == 0 ? qrb::tc_update_launches(batch, n, k, c0) : 1;
+  };
+  int64_t total = np;
+  for (int p = 0; p < np; ++p) {
+    const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
+    if (k + b < n) total += update(k, k + b);
+    if (with_q) total += update(k, k);
+  }
+  return total;
+}
+
 // ---- host-buffer pipeline -------------------------------------------------------
 // The batch is cut into chunks that cycle through kSlots device slots; per chunk the
 // copy-in stream moves A to the slot, the compute stream factors it in place (and
@@ -305,6 +321,11 @@ int qrb_device_error(void) { return qrb::take_device_error(); }
 size_t qrb_workspace_size(int64_t batch, int n) {
   if (batch < 0 || n < 1 || n > QRB_MAX_N) return 0;
   return ws_bytes(batch, n);
+}
+
+int64_t qrb_kernel_launches(int64_t batch, int n, int with_q) {
+  if (batch <= 0 || n < 1 || n > QRB_MAX_N) return 0;
+  return count_launches(batch, n, with_q != 0);
 }
 
 int qrb_geqrf_f32(const float* A, float* H, float* tau, int64_t batch, int n, void* workspace,

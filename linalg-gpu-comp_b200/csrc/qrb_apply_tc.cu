@@ -618,6 +618,25 @@ size_t tc_ws_floats(int64_t batch, int n) {
 
 namespace {
 
+// Row chunks of the W^T reduction: up to ~6 waves of CTAs at 4 per SM, but never chunks
+// under 512 rows (short chunks cost more in partial traffic and in the w2 sum than they
+// gain in balance; measured on b512_n256, b256_n512, b32_n2048).
+struct SplitPlan {
+  int nsplit, chunk;
+};
+
+SplitPlan split_plan(int64_t batch, int n, int k, int c0) {
+  const int m = n - k;
+  const int64_t units = (int64_t)((n - c0 + kTN - 1) / kTN) * batch;
+  int nsplit = (int)((3552 + units - 1) / units);
+  nsplit = nsplit < 1 ? 1 : (nsplit > kMaxSplit ? kMaxSplit : nsplit);
+  const int max_split = (m + 511) / 512;
+  if (nsplit > max_split) nsplit = max_split < 1 ? 1 : max_split;
+  int chunk = (m + nsplit - 1) / nsplit;
+  chunk = (chunk + kR1 - 1) / kR1 * kR1;
+  return {(m + chunk - 1) / chunk, chunk};
+}
+
 template <bool IDENT>
 cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const CUtensorMap& s128,
                          const CUtensorMap& h128, const CUtensorMap& v128, const CUtensorMap& w, const float* T,
@@ -638,17 +657,9 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   const int m = n - k;
   const int nstrips = (n - c0 + kTN - 1) / kTN;
   const int ntiles = (m + kR3 - 1) / kR3;
-  // Row chunks for the W^T reduction: up to ~8 waves of CTAs at 3 per SM, but never
-  // chunks under 512 rows (short chunks cost more in partial traffic and in the w2
-  // sum than they gain in balance; measured on b512_n256, b256_n512, b32_n2048).
   const int64_t units = (int64_t)nstrips * batch;
-  int nsplit = (int)((3552 + units - 1) / units);
-  nsplit = nsplit < 1 ? 1 : (nsplit > kMaxSplit ? kMaxSplit : nsplit);
-  const int max_split = (m + 511) / 512;
-  if (nsplit > max_split) nsplit = max_split < 1 ? 1 : max_split;
-  int chunk = (m + nsplit - 1) / nsplit;
-  chunk = (chunk + kR1 - 1) / kR1 * kR1;
-  nsplit = (m + chunk - 1) / chunk;
+  const SplitPlan sp = split_plan(batch, n, k, c0);
+  const int nsplit = sp.nsplit, chunk = sp.chunk;
   wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(
       s32, v32, part, T, w2, batch, n, k, b, c0, nstrips, chunk, nsplit, trans_t);
   e = cudaGetLastError();
@@ -695,6 +706,10 @@ cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, fl
                                             b, c0, trans_t, store_to_h, s)
                        : launch_split<false>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
                                              b, c0, trans_t, store_to_h, s);
+}
+
+int tc_update_launches(int64_t batch, int n, int k, int c0) {
+  return split_plan(batch, n, k, c0).nsplit > 1 ? 3 : 2;
 }
 
 int take_device_error() {

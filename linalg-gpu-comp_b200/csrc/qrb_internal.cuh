@@ -87,6 +87,8 @@ bool apply_tc_supported(int n);
 cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C,
                             int64_t batch, int n, int k, int b, int c0, int trans_t,
                             int identity_fill, float* tcws, cudaStream_t s);
+// Kernels one launch_apply_tc enqueues: wpart, w2 (only with a split W^T reduction), update.
+int tc_update_launches(int64_t batch, int n, int k, int c0);
 
 // First error code recorded by a kernel whose bounded wait ran out (0 = none); clears it.
 int take_device_error();

@@ -27,6 +27,7 @@ SIGNATURES = {
     "qrb_last_error": (ctypes.c_int, [ctypes.c_char_p, _c_size]),
     "qrb_workspace_size": (_c_size, [_c_int64, ctypes.c_int]),
     "qrb_device_error": (ctypes.c_int, []),
+    "qrb_kernel_launches": (_c_int64, [_c_int64, ctypes.c_int, ctypes.c_int]),
     "qrb_geqrf_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_orgqr_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_qr_f32": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),

@@ -28,7 +28,7 @@ def test_header_declares_the_api():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
         "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error",
-        "qrb_host_workspace_size", "qrb_qr_f32_host"}
+        "qrb_host_workspace_size", "qrb_qr_f32_host", "qrb_kernel_launches"}
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -93,6 +93,23 @@ def test_empty_batch_is_a_no_op(lib):
     # batch == 0 returns before any CUDA call, so it succeeds without a device.
     assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 0, 32, None, 0, None) == 0
     assert lib.qrb_qr_f32(FAKE, FAKE, FAKE, FAKE + 256, 0, 300, None, 0, None) == 0
+
+
+def test_kernel_launch_count(lib):
+    """qrb_kernel_launches mirrors the dispatch: one fused kernel for n <= 64; otherwise a
+    panel per 32 columns and, per block update, wpart + update (+ w2 when the W^T
+    reduction is split over row chunks, i.e. blocks taller than 512 rows at small batch),
+    or one SIMT launch when n % 4 != 0."""
+    assert lib.qrb_kernel_launches(4096, 64, 1) == 1
+    assert lib.qrb_kernel_launches(7, 1, 0) == 1
+    assert lib.qrb_kernel_launches(1, 256, 1) == 8 + (7 + 8) * 2
+    assert lib.qrb_kernel_launches(1, 256, 0) == 8 + 7 * 2
+    assert lib.qrb_kernel_launches(1, 258, 1) == 9 + 8 + 9
+    n32 = lib.qrb_kernel_launches(32, 2048, 1)
+    assert 64 + 127 * 2 < n32 <= 64 + 127 * 3
+    assert lib.qrb_kernel_launches(4096, 2048, 1) == 64 + 127 * 2   # wide batch: no split
+    assert lib.qrb_kernel_launches(0, 256, 1) == 0
+    assert lib.qrb_kernel_launches(1, 5000, 1) == 0
 
 
 def test_compiled_call_path_loads():
