@@ -366,20 +366,15 @@ tiny_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __rest
       if (j < n) {
         const float alpha = __shfl_sync(kFull, a[j], j);
         float x[32];
-        float t0 = 0.f, t1 = 0.f, d0 = 0.f, d1 = 0.f;
+        float t[4] = {0.f, 0.f, 0.f, 0.f}, d[4] = {0.f, 0.f, 0.f, 0.f};   // 4 chains
 #pragma unroll
         for (int r = j + 1; r < 32; ++r) {
           x[r] = __shfl_sync(kFull, a[r], j);
-          if ((r - j) & 1) {
-            t0 = fmaf(x[r], x[r], t0);
-            d0 = fmaf(x[r], a[r], d0);
-          } else {
-            t1 = fmaf(x[r], x[r], t1);
-            d1 = fmaf(x[r], a[r], d1);
-          }
+          t[r & 3] = fmaf(x[r], x[r], t[r & 3]);
+          d[r & 3] = fmaf(x[r], a[r], d[r & 3]);
         }
-        const Reflector f = make_reflector(alpha, t0 + t1, j == n - 1);
-        const float w = fmaf(f.v0, a[j], d0 + d1);   // u^T a_c
+        const Reflector f = make_reflector(alpha, (t[0] + t[1]) + (t[2] + t[3]), j == n - 1);
+        const float w = fmaf(f.v0, a[j], (d[0] + d[1]) + (d[2] + d[3]));   // u^T a_c
         const float coef = lane > j ? f.tau * f.inv_v0 * f.inv_v0 * w : 0.f;
         a[j] = fmaf(-coef, f.v0, a[j]);
 #pragma unroll
@@ -412,14 +407,13 @@ tiny_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __rest
       if (j < n) {
         const float tj = __shfl_sync(kFull, my_tau, j);
         float v[32];
-        float w0 = q[j], w1 = 0.f;   // v_j = 1
+        float w[4] = {q[j], 0.f, 0.f, 0.f};   // v_j = 1; 4 chains
 #pragma unroll
         for (int r = j + 1; r < 32; ++r) {
           v[r] = __shfl_sync(kFull, a[r], j);
-          if ((r - j) & 1) w1 = fmaf(v[r], q[r], w1);
-          else w0 = fmaf(v[r], q[r], w0);
+          w[r & 3] = fmaf(v[r], q[r], w[r & 3]);
         }
-        const float c = tj * (w0 + w1);
+        const float c = tj * ((w[0] + w[1]) + (w[2] + w[3]));
         q[j] -= c;
 #pragma unroll
         for (int r = j + 1; r < 32; ++r) q[r] = fmaf(-c, v[r], q[r]);
