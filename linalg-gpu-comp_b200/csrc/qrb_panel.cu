@@ -7,8 +7,8 @@
 // Gram/solve T^{-1} construction (submission.py:434-448).
 //
 // Layout.  Lane c of every warp owns panel column c; warp w and register i give
-// CTA-local row w + 8i, so a CTA of 8 warps holds 8*RPT rows in registers and a
-// cluster of CL CTAs (rank q) holds rows [q*8*RPT, (q+1)*8*RPT).  Step j:
+// CTA-local row w + W*i, so a CTA of W warps holds W*RPT rows in registers and a
+// cluster of CL CTAs (rank q) holds rows [q*W*RPT, (q+1)*W*RPT).  Step j:
 //   1. every lane fetches column j of its rows with one shuffle per row and forms
 //      partial ||x||^2 / alpha (identical in all lanes of a warp);
 //   2. the per-warp partials are combined across warps (and, for CL > 1, across
@@ -28,16 +28,15 @@ namespace cg = cooperative_groups;
 namespace qrb {
 namespace {
 
-constexpr int kPanelWarps = 8;
-constexpr int kPanelThreads = kPanelWarps * 32;
 
-template <int RPT, int CL>
-__global__ void __launch_bounds__(kPanelThreads)
+template <int RPT, int CL, int W>
+__global__ void __launch_bounds__(W * 32)
 panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __restrict__ tau,
              float* __restrict__ Tout, int n, int k, int b) {
-  constexpr int kRowsCta = kPanelWarps * RPT;
-  __shared__ float2 red_n[2][kPanelWarps];        // per-warp (tail^2, alpha) partials
-  __shared__ float red_w[2][kPanelWarps][32];     // per-warp d_c partials
+  constexpr int kPanelWarps = W;
+  constexpr int kRowsCta = W * RPT;
+  __shared__ float2 red_n[2][W];                  // per-warp (tail^2, alpha) partials
+  __shared__ float red_w[2][W][32];               // per-warp d_c partials
   __shared__ float rowj[2][32];                   // row j of the panel (rank 0)
   __shared__ float2 cred_n[2][CL];                // per-CTA partials (CL > 1)
   __shared__ float cred_w[2][CL][32];
@@ -57,7 +56,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   float a[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    const int pr = row0 + 8 * i;
+    const int pr = row0 + W * i;
     a[i] = (pr < m && lane < b) ? __ldg(src + moff + (size_t)(k + pr) * n + k + lane) : 0.f;
   }
 
@@ -66,7 +65,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   // column and divides it by v0_c once at the end.  Only registers i < kTop can hold
   // a row <= 31 (rank 0); every other row is below any pivot of the panel and needs no
   // row predicate.
-  constexpr int kTop = 4;
+  constexpr int kTop = 32 / W;
   float my_inv = 1.f, my_beta = 0.f;   // this lane's column reflector (set at step j == lane)
   for (int j = 0; j < b; ++j) {
     const int par = j & 1;
@@ -77,7 +76,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     float tail = 0.f, tail2 = 0.f, alpha = 0.f, d0 = 0.f, d1 = 0.f, ajc = 0.f;
 #pragma unroll
     for (int i = 0; i < RPT; ++i) {
-      const int pr = row0 + 8 * i;
+      const int pr = row0 + W * i;
       const float x = __shfl_sync(0xffffffffu, a[i], j);
       u[i] = x;
       if (i < kTop) {
@@ -98,7 +97,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     // ---- 2. one reduction round (double-buffered: one barrier per step suffices) ----
     if (lane == 0) red_n[par][warp] = make_float2(tail, alpha);
     red_w[par][warp][lane] = d0 + d1;
-    if (rank == 0 && warp == (j & (kPanelWarps - 1))) rowj[par][lane] = ajc;   // row j: warp j % 8
+    if (rank == 0 && warp == (j & (kPanelWarps - 1))) rowj[par][lane] = ajc;   // row j: warp j % W
     __syncthreads();
     float2 nsum = make_float2(0.f, 0.f);
     float dsum = 0.f, aj;
@@ -146,7 +145,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
     const float w = fmaf(f.v0, aj, dsum);   // u^T a_c with u = (0.., v0, x_{j+1}, ..)
 #pragma unroll
     for (int i = 0; i < kTop && i < RPT; ++i) {
-      const int pr = row0 + 8 * i;
+      const int pr = row0 + W * i;
       u[i] = pr > j ? u[i] : (pr == j ? f.v0 : 0.f);
     }
 
@@ -199,7 +198,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   // ---- write back panel (v = raw / v0 below, beta on the diagonal) and T ------
 #pragma unroll
   for (int i = 0; i < RPT; ++i) {
-    const int pr = row0 + 8 * i;
+    const int pr = row0 + W * i;
     float h = a[i] * my_inv;
     if (i < kTop) h = pr > lane ? h : (pr == lane ? my_beta : a[i]);
     if (pr < m && lane < b) H[moff + (size_t)(k + pr) * n + k + lane] = h;
@@ -213,12 +212,12 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   if constexpr (CL > 1) cg::this_cluster().sync();   // no CTA exits while peers may still write to it
 }
 
-template <int RPT, int CL>
+template <int RPT, int CL, int W = 8>
 cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int64_t batch,
                            int n, int k, int b, cudaStream_t s) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(batch * CL));
-  cfg.blockDim = dim3(kPanelThreads);
+  cfg.blockDim = dim3(W * 32);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -228,7 +227,7 @@ cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL>, src, H, tau, T, n, k, b);
+  return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL, W>, src, H, tau, T, n, k, b);
 }
 
 }  // namespace
@@ -239,8 +238,15 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T, int64
   const int m = n - k;
   // Single CTA while the panel fits 8 warps x 64 rows; clusters of 256-row CTAs
   // (512-row for m > 2048) beyond that.
-  if (m <= 64) return launch_panel_t<8, 1>(src, H, tau, T, batch, n, k, b, s);
-  if (m <= 128) return launch_panel_t<16, 1>(src, H, tau, T, batch, n, k, b, s);
+  // Short panels: with many matrices in flight (throughput-bound) fewer warps with more
+  // rows each cost less per column (fewer partials, cheaper barrier); a small batch is
+  // latency-bound and does better spread over 8 warps.  Measured on one B200: b512_n256
+  // 1.54 vs 1.59 ms, b40_n176 0.218 vs 0.210 ms.
+  const bool wide = batch >= 256;
+  if (m <= 64) return wide ? launch_panel_t<32, 1, 2>(src, H, tau, T, batch, n, k, b, s)
+                           : launch_panel_t<8, 1>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 128) return wide ? launch_panel_t<32, 1, 4>(src, H, tau, T, batch, n, k, b, s)
+                            : launch_panel_t<16, 1>(src, H, tau, T, batch, n, k, b, s);
   if (m <= 256) return launch_panel_t<32, 1>(src, H, tau, T, batch, n, k, b, s);
   if (m <= 512) return launch_panel_t<64, 1>(src, H, tau, T, batch, n, k, b, s);
   if (m <= 1024) return launch_panel_t<32, 4>(src, H, tau, T, batch, n, k, b, s);
