@@ -9,15 +9,17 @@
 // shared memory into two tf32 pieces (x = x0 + x1, exact to 2^-22 |x|) and
 // tcgen05.mma kind::tf32 accumulates x1y0 + x0y1 + x0y0, smallest first.  The QR
 // residuals measured against the fp32 checker are within 5% of those of a three-piece,
-// six-product split (which costs 15-20% more time at n >= 256).  Operands travel through HBM as plain fp32 (V straight from H, masked to
-// the unit lower trapezoid where it is split).  Three launches per panel:
+// six-product split (which costs 15-20% more time at n >= 256).  Operands travel
+// through HBM as plain fp32 (V straight from H, masked to the unit lower trapezoid
+// where it is split).  Two or three launches per panel:
 //   wpart_kernel   W^T (64 x 32) = C^T V for a 64-column strip over one row chunk:
 //                  TMA streams 32-row stages of C and V (MN-major operands, which
 //                  for tf32 take the 128-byte swizzle with 32-byte atoms), threads
 //                  split both, one thread issues M=64 N=32 K=8 MMAs into one TMEM
 //                  accumulator per stage, stage partials are summed in registers;
-//   w2_kernel      W = sum of the chunk partials (fixed order), W2 = op(T) W in fp32,
-//                  in the K-major layout of the next step;
+//                  with a single row chunk it also forms W2 = op(T) W itself;
+//   w2_kernel      only with several row chunks: W = sum of the chunk partials (fixed
+//                  order), W2 = op(T) W in fp32, in the K-major layout of the next step;
 //   update_kernel  C -= V W2 by persistent warp-specialised CTAs: per 128-row
 //                  tile, M=128 N=64 K=32 MMAs into double-buffered TMEM, the
 //                  epilogue subtracts from the TMA-loaded C tile and TMA-stores it.
