@@ -112,6 +112,22 @@ def test_kernel_launch_count(lib):
     assert lib.qrb_kernel_launches(1, 5000, 1) == 0
 
 
+def test_kernel_launch_count_bounds(lib):
+    """For every n the count is one fused launch (n <= 64) or np panels plus 1 (SIMT),
+    2 or 3 (tensor core) launches per block update; geqrf alone has np - 1 updates."""
+    for n in range(1, 4097):
+        for batch in (1, 7, 64, 640, 4096):
+            full, geqrf = lib.qrb_kernel_launches(batch, n, 1), lib.qrb_kernel_launches(batch, n, 0)
+            if n <= 64:
+                assert full == geqrf == 1
+                continue
+            np_ = (n + 31) // 32
+            lo, hi = (1, 1) if n % 4 else (2, 3)
+            assert np_ + lo * (2 * np_ - 1) <= full <= np_ + hi * (2 * np_ - 1), (batch, n, full)
+            assert np_ + lo * (np_ - 1) <= geqrf <= np_ + hi * (np_ - 1), (batch, n, geqrf)
+            assert geqrf < full
+
+
 def test_compiled_call_path_loads():
     """The compiled torch call path (qr_b200/_entry.cpp) is built next to the library,
     links it, and exposes the two hot calls (no GPU needed to load it)."""
