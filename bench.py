@@ -196,8 +196,9 @@ def cpu_baseline(config: str, seed: int, budget_s: float = 12.0) -> dict:
 
 
 def run_reference(args) -> dict | None:
-    dist, rank, world, local = dist_init(args.gpus)
-    if rank != 0:
+    # CPU work on rank 0 only; the other torchrun ranks exit without work.  No process
+    # group is needed (nothing is exchanged), so this arm does not touch CUDA at all.
+    if int(os.environ.get("RANK", "0")) != 0:
         return None
     from oracle import cpu_ref
     from qr_b200.inputs import CONFIGS

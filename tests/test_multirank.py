@@ -59,3 +59,28 @@ def test_bench_accounting():
     # n = 2048 at batch 32: tall blocks split the W^T reduction and add the w2 sum
     assert 64 + 127 * 2 < bench.kernel_launches(2048, 32) <= 64 + 127 * 3
     assert bench.kernel_launches(258) == 9 + (8 + 9)              # n % 4 != 0: one SIMT launch per update
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """`bench.py --impl reference` launched by torchrun with two ranks: rank 0 times the CPU
+    reference and prints one JSON line, the other rank exits 0 without work (no GPU needed)."""
+    import json
+    import socket
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), str(root / "bench.py"),
+           "--impl", "reference", "--gpus", "2", "--config", "b64_n32", "--steps", "1", "--warmup", "1"]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=root)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(l) for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1, r.stdout
+    d = lines[0]
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "reference"
