@@ -5,20 +5,28 @@
 
 One step = one fused QR (``qr_b200.qr``: (H, tau) in torch.geqrf form plus the
 explicit Q, i.e. 8/3 n^3 flops per matrix) of one batch of the configuration.
-Default configuration: ``b4096_n64`` (4096 i.i.d. N(0,1) 64x64 fp32 matrices).
+Default configuration: ``b32_n2048`` (32 i.i.d. N(0,1) 2048x2048 fp32 matrices,
+the largest configuration; the tensor-core blocked path).  The other four
+configurations are timed after it (fewer steps) and reported under
+``extra_configs`` in the same JSON line.
 
-Multi-GPU (torchrun, one process per GPU): weak scaling -- every rank factors its
-own full batch (seed + rank); there is no collective on the data path, only a
-barrier and a max-reduction of the timings.  ``value`` = all ranks' matrices /
-max-over-ranks time.
+Multi-GPU (torchrun, one process per GPU): the configuration's batch is split
+into contiguous slices, rank r factoring matrices [r*B/N, (r+1)*B/N) of the same
+seeded batch (strong scaling; uneven tails go to the later ranks).  There is no
+collective on the data path, only a barrier and a max-reduction of the timings.
+``value`` = B / max-over-ranks time.
 
 Timing: per step, the L2 is flushed (256 MiB write, untimed, as the reference
 harness's clear_l2_cache does) and the step is bracketed by CUDA events on the
 launching stream; ms_per_step is the mean of the K step durations, max over ranks.
+A second pass of the same K steps runs with the library's per-launch CUDA-event
+timing on (``qrb_kernel_timing``); its per-kernel totals give the dominant kernel
+and its roofline.
 
 ``--impl reference``: the reference arm -- CPU ``torch.linalg.qr`` (the
-comparator the reference names) on the host cores, rank 0 only, one bounded
-sample of the workload per step.
+comparator the reference names) on all host cores, rank 0 only, on the full batch
+of the configuration every step.  It imports nothing that loads the repo's
+libraries.
 """
 from __future__ import annotations
 
@@ -41,7 +49,7 @@ import torch  # noqa: E402
 
 METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "BASELINE.json").exists() \
     else "batched QR matrices/s"
-DEFAULT_CONFIG = "b4096_n64"
+DEFAULT_CONFIG = "b32_n2048"
 
 
 def flops_per_matrix(n: int) -> float:
@@ -53,23 +61,19 @@ def bytes_per_matrix(n: int) -> int:
     return 12 * n * n + 4 * n
 
 
-def kernel_launches(n: int, batch: int = 1) -> int:
-    """libqrb200 kernels one fused QR enqueues, as the library itself counts them
-    (qrb_kernel_launches mirrors its dispatch in csrc/qrb_api.cu)."""
-    import qr_b200
-    return int(qr_b200.lib().qrb_kernel_launches(batch, n, 1))
-
-
-def dominant_kernel(n: int) -> str:
-    return "small_qr_kernel" if n <= 64 else "wpart_kernel"
-
-
 def load_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
-    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def shard(batch: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous slice [lo, hi) of a batch of ``batch`` matrices owned by ``rank`` of
+    ``world`` ranks; sizes differ by at most one, the larger slices last."""
+    return rank * batch // world, (rank + 1) * batch // world
 
 
 def load_traffic(config: str):
@@ -196,16 +200,20 @@ def cpu_baseline(config: str, seed: int, budget_s: float = 12.0) -> dict:
 
 
 def run_reference(args) -> dict | None:
-    # CPU work on rank 0 only; the other torchrun ranks exit without work.  No process
-    # group is needed (nothing is exchanged), so this arm does not touch CUDA at all.
+    """CPU torch.linalg.qr on the full batch of the configuration, every step.
+
+    Rank 0 only; the other torchrun ranks exit without work.  No process group is
+    needed (nothing is exchanged), CUDA is never touched, and only ``qr_b200.inputs``
+    (plain torch generators) is imported from the package -- no repo library loads."""
     if int(os.environ.get("RANK", "0")) != 0:
         return None
     from oracle import cpu_ref
-    from qr_b200.inputs import CONFIGS
+    from qr_b200.inputs import CONFIGS, config_input
     batch, n, _ = CONFIGS[args.config]
     threads = cpu_ref.set_threads()
-    m, A = cpu_sample(args.config, args.seed, 0.12)      # ~0.12 s of CPU work per step
-    for _ in range(args.warmup):
+    A = config_input(args.config, seed=args.seed, device="cpu")
+    warm = max(1, min(args.warmup, 3))
+    for _ in range(warm):
         cpu_ref.cpu_qr(A)
     t = []
     for _ in range(args.steps):
@@ -213,15 +221,15 @@ def run_reference(args) -> dict | None:
         cpu_ref.cpu_qr(A)
         t.append(time.perf_counter() - t0)
     ms = 1e3 * statistics.mean(t)
-    value = m / (ms / 1e3)
-    sample = (f"torch.linalg.qr (LAPACK sgeqrf+sorgqr, fp32) on {m} of the {batch} {args.config} "
-              f"matrices per step, {threads} host threads")
+    value = batch / (ms / 1e3)
+    sample = (f"torch.linalg.qr (LAPACK sgeqrf+sorgqr, fp32) on the full batch of {batch} {args.config} "
+              f"matrices per step, {threads} host threads, {warm} untimed warm-up call(s)")
     return {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "matrices/s",
         "gflops": value * flops_per_matrix(n) / 1e9, "n_gpus": args.gpus, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded",
-        "config": {"workload": args.config, "batch": batch, "n": n, "sample_matrices": m},
+        "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded (CPU generator)",
+        "config": {"workload": args.config, "batch": batch, "n": n, "sample_matrices": batch},
         "cpu_baseline": {"value": value, "unit": "matrices/s", "cores": threads, "kind": "reference",
                          "sample": sample},
         "e2e": {"value": value, "unit": "matrices/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -231,41 +239,123 @@ def run_reference(args) -> dict | None:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
-def run_ours(args) -> dict | None:
+def time_steps(step, steps: int, stream, flush, dist, dev, clocks=None) -> float:
+    """Mean CUDA-event duration of ``steps`` calls of ``step`` (L2 flushed before each,
+    outside the events), max over ranks."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier(dist, dev)
+    for i in range(steps):
+        flush.fill_(42)
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    barrier(dist, dev)
+    times = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    return reduce_max(dist, statistics.mean(times), dev)
+
+
+def kernel_profile(step, steps: int, stream, flush, dist, dev) -> dict:
+    """Per-kernel CUDA-event totals over ``steps`` more steps, with the library's launch
+    timing on (events on each kernel's launching stream)."""
+    import qr_b200
+    from qr_b200._lib import kernel_timing_report
+    lib = qr_b200.lib()
+    kernel_timing_report()            # drop anything logged earlier
+    barrier(dist, dev)
+    lib.qrb_kernel_timing(1)
+    try:
+        for _ in range(steps):
+            flush.fill_(7)
+            step()
+        torch.cuda.synchronize(dev)
+    finally:
+        lib.qrb_kernel_timing(0)
+    return kernel_timing_report()
+
+
+def roofline_from_profile(prof: dict, steps: int, step_ms: float, n: int, batch: int, peaks: dict,
+                          traffic) -> dict | None:
+    if not prof:
+        return None
+    total = sum(v["ms"] for v in prof.values())
+    name, d = max(prof.items(), key=lambda kv: kv[1]["ms"])
+    per_launch_ms = d["ms"] / d["launches"]
+    bytes_per_launch = d["bytes"] / d["launches"]
+    gbs = d["bytes"] / (d["ms"] / 1e3) / 1e9
+    tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
+    # 3xTF32: the tensor-core kernels issue three tf32 products per useful multiply-add.
+    tensor_kernel = name in ("wpart_kernel", "update_kernel", "ygemm_kernel", "wupdate_kernel")
+    k_tflops = (3.0 if tensor_kernel else 1.0) * d["flops"] / (d["ms"] / 1e3) / 1e12
+    step_tflops = batch * flops_per_matrix(n) / (step_ms / 1e3) / 1e12
+    return {
+        "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": gbs / peaks["hbm_gbs"], "traffic": traffic, "kernel": name,
+        "launches_per_step": d["launches"] / steps, "ms_per_launch": per_launch_ms,
+        "algorithmic_bytes_per_launch": bytes_per_launch,
+        "share_of_kernel_time": d["ms"] / total if total > 0 else None,
+        "peak_source": f"{peaks['source']} hbm_gbs (MEASURED_PEAKS.json), 'of measured'",
+        "tensor": {"kernel_tflops_issued": k_tflops, "step_tflops_useful": step_tflops,
+                   "peak_tf32_derived": tf32_peak,
+                   "kernel_frac": k_tflops / tf32_peak if tensor_kernel else None,
+                   "step_frac": step_tflops / tf32_peak,
+                   "note": "tf32 peak derived as bf16_tflops_sustained / 2 (no tf32 GEMM is measured); "
+                           "kernel figure counts the three tf32 products of 3xTF32"},
+        "kernels": {k: {"launches_per_step": v["launches"] / steps, "ms_per_step": v["ms"] / steps,
+                        "share": v["ms"] / total if total > 0 else None,
+                        "gbs": v["bytes"] / (v["ms"] / 1e3) / 1e9 if v["ms"] > 0 else None}
+                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1]["ms"])},
+    }
+
+
+def bench_config(config: str, args, dist, rank: int, world: int, dev, steps: int, warmup: int,
+                 flush, clocks=None) -> dict:
+    """Time one configuration with this rank's slice of its batch; returns the numbers."""
     import qr_b200
     from qr_b200.inputs import CONFIGS, config_input
+    batch, n, _ = CONFIGS[config]
+    lo, hi = shard(batch, rank, world)
+    full = config_input(config, seed=args.seed, device=dev)
+    A = full[lo:hi].contiguous()
+    del full
+    H = torch.empty_like(A)
+    tau = torch.empty(A.shape[0], n, device=dev)
+    Q = torch.empty_like(A)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        if A.shape[0] > 0:
+            qr_b200.qr(A, out=(H, tau, Q))
+
+    for _ in range(max(warmup, 3)):
+        step()
+    if clocks is not None:
+        with clocks:
+            ms = time_steps(step, steps, stream, flush, dist, dev)
+    else:
+        ms = time_steps(step, steps, stream, flush, dist, dev)
+    prof = kernel_profile(step, steps, stream, flush, dist, dev)
+    return {"batch": batch, "n": n, "lo": lo, "hi": hi, "ms": ms, "prof": prof, "A": A, "H": H, "tau": tau,
+            "Q": Q, "step": step}
+
+
+def run_ours(args) -> dict | None:
+    import qr_b200
 
     dist, rank, world, local = dist_init(args.gpus)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    batch, n, kind = CONFIGS[args.config]
-    A = config_input(args.config, seed=args.seed + rank, device=dev)
-    H = torch.empty_like(A)
-    tau = torch.empty(batch, n, device=dev)
-    Q = torch.empty_like(A)
     flush = torch.empty(256 * 1024 * 1024 // 8, dtype=torch.int64, device=dev)
     stream = torch.cuda.current_stream(dev)
+    peaks = load_peaks()
 
-    def step():
-        qr_b200.qr(A, out=(H, tau, Q))
-
-    for _ in range(max(args.warmup, 3)):
-        step()
-    barrier(dist, dev)
-
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(dev.index) as clocks:
-        barrier(dist, dev)
-        for i in range(args.steps):
-            flush.fill_(42)                      # L2 flush, outside the events
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        barrier(dist, dev)
-    times = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    ms_local = statistics.mean(times)
-    ms = reduce_max(dist, ms_local, dev)
+    clocks = ClockSampler(dev.index)
+    main = bench_config(args.config, args, dist, rank, world, dev, args.steps, args.warmup, flush, clocks)
+    batch, n, ms = main["batch"], main["n"], main["ms"]
+    A, H, tau, Q = main["A"], main["H"], main["tau"], main["Q"]
+    roof = roofline_from_profile(main["prof"], args.steps, ms, n, main["hi"] - main["lo"], peaks,
+                                 load_traffic(args.config))
+    launches = sum(v["launches"] for v in main["prof"].values())
 
     # end to end through the public API: pinned host A -> device, QR, H/tau/Q -> pinned host
     e2e = None
@@ -277,7 +367,8 @@ def run_ours(args) -> dict | None:
 
         def e2e_step():
             # one library call: chunked host->device copy, QR, device->host copies
-            qr_b200.qr_host(A_h, out=(H_h, t_h, Q_h), device=dev)
+            if A_h.shape[0] > 0:
+                qr_b200.qr_host(A_h, out=(H_h, t_h, Q_h), device=dev)
 
         for _ in range(2):
             e2e_step()
@@ -292,9 +383,27 @@ def run_ours(args) -> dict | None:
         ms_e2e = reduce_max(dist, ev0.elapsed_time(ev1) / k_e2e, dev)
         h2d = A.numel() * 4
         d2h = (H.numel() + tau.numel() + Q.numel()) * 4
-        e2e = {"value": world * batch / (ms_e2e / 1e3), "unit": "matrices/s",
+        e2e = {"value": batch / (ms_e2e / 1e3), "unit": "matrices/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms_e2e,
                "steps": k_e2e, "api": "qr_b200.qr_host (C ABI qrb_qr_f32_host, pinned host buffers)"}
+        del A_h, H_h, t_h, Q_h
+    del main, A, H, tau, Q
+
+    extras = {}
+    if not args.no_extra:
+        from qr_b200.inputs import CONFIGS
+        for name in CONFIGS:
+            if name == args.config:
+                continue
+            r = bench_config(name, args, dist, rank, world, dev, max(3, min(args.steps, 10)), 3, flush)
+            extras[name] = {
+                "ms_per_step": r["ms"], "matrices_per_s": r["batch"] / (r["ms"] / 1e3),
+                "gflops": r["batch"] * flops_per_matrix(r["n"]) / (r["ms"] / 1e3) / 1e9,
+                "steps": max(3, min(args.steps, 10)),
+                "roofline": roofline_from_profile(r["prof"], max(3, min(args.steps, 10)), r["ms"], r["n"],
+                                                  r["hi"] - r["lo"], peaks, load_traffic(name)),
+            }
+            del r
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -302,38 +411,21 @@ def run_ours(args) -> dict | None:
 
     if rank != 0:
         return None
-    peaks = load_peaks()
-    value = world * batch / (ms / 1e3)
-    alg_bytes = batch * bytes_per_matrix(n)
-    kdur_s = ms_local / 1e3 if kernel_launches(n) == 1 else None
-    roof = None
-    if kdur_s is None:
-        # Blocked path: many launches per step; report the step against the dense tf32
-        # tensor rate (the tensor-core updates carry the n^3 work).  No tf32 peak is
-        # measured here: half the measured bf16 GEMM rate stands in for it.
-        tf = value / world * flops_per_matrix(n) / 1e12
-        peak = peaks["bf16_tflops"] / 2.0
-        roof = {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
-                "traffic": None, "kernel": "whole step (panels + tcgen05 updates), 8/3 n^3 per matrix",
-                "peak_source": f"{peaks['source']} bf16_tflops / 2 (tf32 rate) from MEASURED_PEAKS.json"}
-    if kdur_s is not None:
-        ach = alg_bytes / kdur_s / 1e9
-        traffic = load_traffic(args.config)
-        roof = {"bound": "hbm", "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": ach / peaks["hbm_gbs"], "traffic": traffic, "kernel": dominant_kernel(n),
-                "algorithmic_bytes_per_launch": alg_bytes,
-                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)"}
+    value = batch / (ms / 1e3)
     return {
         "metric": METRIC, "value": value, "unit": "matrices/s",
         "gflops": value * flops_per_matrix(n) / 1e9, "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded per rank",
-        "config": {"workload": args.config, "batch_per_gpu": batch, "n": n, "global_batch": world * batch,
-                   "parallelism": f"batch-sharded x{world}, no collective", "l2": "flushed between steps (256 MiB write)",
-                   "op": "geqrf + orgqr (qrb_qr_f32)"},
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic i.i.d. N(0,1), seeded; one batch split across ranks",
+        "config": {"workload": args.config, "global_batch": batch, "n": n,
+                   "batch_per_gpu": [shard(batch, r, world)[1] - shard(batch, r, world)[0] for r in range(world)],
+                   "parallelism": f"batch split over {world} GPU(s), no collective",
+                   "l2": "flushed between steps (256 MiB write)", "op": "geqrf + orgqr (qrb_qr_f32)"},
         "roofline": roof, "cpu_baseline": cpu, "e2e": e2e,
-        "gpu_launches": kernel_launches(n, batch) * args.steps,
+        "gpu_launches": int(round(launches)),
+        "gpu_launches_note": "kernels the library launched in the K timed-pass steps, counted by its launch log",
         "clocks": clocks.summary(),
+        "extra_configs": extras,
     }
 
 
@@ -416,6 +508,7 @@ def main(argv=None):
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="skip the other configurations")
     ap.add_argument("--suite", choices=["gpumode"], default=None,
                     help="gpumode: custom_kernel on the reference task's benchmark shapes (one line each)")
     args = ap.parse_args(argv)

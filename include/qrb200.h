@@ -42,7 +42,8 @@ extern "C" {
 enum qrb_status {
   QRB_OK = 0,
   QRB_ERR_INVALID_ARG = 1,   /* null pointer, n < 1, batch < 0, misaligned pointer */
-  QRB_ERR_UNSUPPORTED = 2,   /* n above QRB_MAX_N */
+  QRB_ERR_UNSUPPORTED = 2,   /* n above QRB_MAX_N, batch above 2^31, or (allocation-free
+                                entry point) a batch larger than its static scratch holds */
   QRB_ERR_WORKSPACE = 3,     /* workspace missing or smaller than qrb_workspace_size() */
   QRB_ERR_CUDA = 4,          /* a CUDA runtime call or kernel launch failed */
   QRB_ERR_DEVICE = 5         /* current device is not an sm_100 (B200-class) GPU */
@@ -96,6 +97,16 @@ QRB_API int qrb_device_error(void);
  * builders and launch accounting; no counterpart in the reference. */
 QRB_API int64_t qrb_kernel_launches(int64_t batch, int n, int with_q);
 
+/* Per-launch kernel timing, off by default.  While enabled, every kernel the library
+ * launches is bracketed by two CUDA events on its launching stream.  The report
+ * waits for the logged events, writes one line per kernel name,
+ *   "<name> <launches> <total ms> <algorithmic bytes> <flops>\n",
+ * into buf (NUL-terminated, truncated to len), clears the log and returns the length
+ * the full report needs (including the NUL).  For profilers and benchmarks; no
+ * counterpart in the reference (its bench scripts time whole calls). */
+QRB_API void qrb_kernel_timing(int enable);
+QRB_API size_t qrb_kernel_timing_report(char* buf, size_t len);
+
 /* (H, tau) = geqrf(A) without any caller workspace, for callers that cannot
  * allocate device memory (a plugin host that passes only raw input/output pointers,
  * or a path that must not enter the allocator).  No counterpart in the reference.
@@ -103,7 +114,9 @@ QRB_API int64_t qrb_kernel_launches(int64_t batch, int n, int with_q);
  * keeps until exit; for n > 64 the batch is limited to 2048 (QRB_ERR_UNSUPPORTED
  * beyond).  All calls share that array: calls that may overlap on the GPU race.
  * The first call on a device looks the array up and should come before any
- * stream capture.  Returns a qrb_status; it does not set qrb_last_error. */
+ * stream capture; the looked-up address is kept for the life of the process, so the
+ * entry point must not be used across a device reset.  Returns a qrb_status and, on
+ * failure, sets the qrb_last_error message. */
 QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch, int n,
                                   void* stream);
 

@@ -36,6 +36,18 @@ int fail(int status, const char* fmt, ...) {
   return status;
 }
 
+}  // namespace
+
+namespace qrb {
+int set_error(int status, const char* msg) {
+  g_last_msg = msg;
+  g_last_status = status;
+  return status;
+}
+}  // namespace qrb
+
+namespace {
+
 int cuda_fail(cudaError_t e, const char* what) {
   return fail(QRB_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
 }

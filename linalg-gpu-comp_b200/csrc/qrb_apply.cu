@@ -203,6 +203,9 @@ cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, 
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   dim3 grid((unsigned)((int64_t)((n - c0 + kTN - 1) / kTN) * batch));
+  const double m = n - k, nc = n - c0;
+  LaunchTimer timer("apply_kernel", s, (double)batch * (8.0 * m * nc + 4.0 * m * b),
+                    (double)batch * 4.0 * m * nc * b);
   apply_kernel<<<grid, kThreads, smem, s>>>(H, T, src, C, n, k, b, c0, trans_t, identity_fill);
   return cudaGetLastError();
 }

@@ -630,7 +630,9 @@ struct SplitPlan {
 SplitPlan split_plan(int64_t batch, int n, int k, int c0) {
   const int m = n - k;
   const int64_t units = (int64_t)((n - c0 + kTN - 1) / kTN) * batch;
-  int nsplit = (int)((3552 + units - 1) / units);
+  // 24 = 4 resident CTAs per SM x 6 waves
+  const int64_t target = 24 * (int64_t)sm_count();
+  int nsplit = (int)((target + units - 1) / units);
   nsplit = nsplit < 1 ? 1 : (nsplit > kMaxSplit ? kMaxSplit : nsplit);
   const int max_split = (m + 511) / 512;
   if (nsplit > max_split) nsplit = max_split < 1 ? 1 : max_split;
@@ -662,11 +664,17 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   const int64_t units = (int64_t)nstrips * batch;
   const SplitPlan sp = split_plan(batch, n, k, c0);
   const int nsplit = sp.nsplit, chunk = sp.chunk;
-  wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(
-      s32, v32, part, T, w2, batch, n, k, b, c0, nstrips, chunk, nsplit, trans_t);
-  e = cudaGetLastError();
+  const double mm = m, nc = n - c0;
+  {
+    LaunchTimer timer("wpart_kernel", st, (double)batch * (4.0 * mm * nc + 4.0 * mm * b * nstrips),
+                      (double)batch * 2.0 * mm * nc * b);
+    wpart_kernel<IDENT><<<(unsigned)(units * nsplit), kThreads, kSmemA, st>>>(
+        s32, v32, part, T, w2, batch, n, k, b, c0, nstrips, chunk, nsplit, trans_t);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   if (nsplit > 1) {
+    LaunchTimer timer("w2_kernel", st, (double)units * (nsplit + 1) * kTN * 32 * 4.0);
     w2_kernel<<<(unsigned)units, 256, 0, st>>>(part, T, w2, batch, n, c0, nstrips, nsplit, trans_t);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
@@ -674,12 +682,15 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   // Persistent update: at least four items per SM so the last round is short; strip
   // groups (each reloading V) only when there are too few row tiles for that.
   const int64_t tiles = batch * ntiles;
-  int ngroups = (int)((4 * 148 + tiles - 1) / tiles);
+  int ngroups = (int)((4 * (int64_t)sm_count() + tiles - 1) / tiles);
   ngroups = ngroups < 1 ? 1 : (ngroups > nstrips ? nstrips : ngroups);
   const int gsize = (nstrips + ngroups - 1) / ngroups;
   ngroups = (nstrips + gsize - 1) / gsize;
   const int64_t items = tiles * ngroups;
-  const unsigned gridb = (unsigned)(items < 148 ? items : 148);
+  const int sms = sm_count();
+  const unsigned gridb = (unsigned)(items < sms ? items : sms);
+  LaunchTimer timer("update_kernel", st, (double)batch * (8.0 * mm * nc + 4.0 * mm * b),
+                    (double)batch * 2.0 * mm * nc * b);
   update_kernel<IDENT><<<gridb, kThreadsB, kSmemB, st>>>(s128, h128, v128, w, batch, n, k, b, c0, nstrips, ntiles,
                                                          ngroups, gsize, store_to_h);
   return cudaGetLastError();

@@ -52,6 +52,30 @@ __device__ __forceinline__ Reflector make_reflector(float alpha, float tail2, bo
   return r;
 }
 
+// ---- host helpers -----------------------------------------------------------
+// Records `msg` as the calling thread's last error (qrb_last_error) and returns status.
+int set_error(int status, const char* msg);
+
+// Streaming multiprocessors of the current device (cached per device).
+int sm_count();
+
+// Brackets one kernel launch with CUDA events on its stream while kernel timing is
+// enabled (qrb_kernel_timing); `bytes` / `flops` are the launch's algorithmic traffic
+// and arithmetic, summed per kernel name in the report.  No-op when timing is off.
+class LaunchTimer {
+ public:
+  LaunchTimer(const char* name, cudaStream_t s, double bytes = 0, double flops = 0);
+  ~LaunchTimer();
+  LaunchTimer(const LaunchTimer&) = delete;
+  LaunchTimer& operator=(const LaunchTimer&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t s_;
+  double bytes_, flops_;
+  cudaEvent_t e0_ = nullptr, e1_ = nullptr;
+};
+
 // ---- launchers (return cudaError_t of the launch) ---------------------------
 // Small-n fused kernel: geqrf and/or orgqr of n <= 64 matrices, one CTA each.
 // mode bit 0: factor A -> (H, tau); bit 1: form Q from (H, tau).

@@ -61,6 +61,7 @@ cudaError_t launch_larft(const float* H, const float* tau, float* T_all, int64_t
                          cudaStream_t s) {
   if (batch == 0) return cudaSuccess;
   dim3 grid((unsigned)((int64_t)((n + kNB - 1) / kNB) * batch));
+  LaunchTimer timer("larft_kernel", s, (double)batch * 2.0 * n * n);
   larft_kernel<<<grid, kThreads, 0, s>>>(H, tau, T_all, batch, n);
   return cudaGetLastError();
 }

@@ -25,7 +25,9 @@
 //     different host threads without ordering) race on the scratch.
 //   * The device address of the array is looked up once per device by the first
 //     call made with that device current (cudaGetSymbolAddress); make that first
-//     call before any stream capture begins.
+//     call before any stream capture begins.  The cached address belongs to the
+//     device's primary context: do not use this entry point across a device reset
+//     (cudaDeviceReset), which would leave the cached address stale.
 #include <atomic>
 #include <mutex>
 
@@ -67,37 +69,49 @@ cudaError_t scratch_address(void** out) {
 
 extern "C" QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* tau, int64_t batch,
                                              int n, void* stream) {
-  // Argument checks mirror qrb_geqrf_f32; the workspace is internal.
-  if (batch < 0 || n < 1) return QRB_ERR_INVALID_ARG;
-  if (n > QRB_MAX_N) return QRB_ERR_UNSUPPORTED;
+  // Argument checks mirror qrb_geqrf_f32; the workspace is internal.  Failures set the
+  // thread's qrb_last_error message like every other entry point.
+  using qrb::set_error;
+  if (batch < 0) return set_error(QRB_ERR_INVALID_ARG, "batch must be >= 0");
+  if (n < 1) return set_error(QRB_ERR_INVALID_ARG, "n must be >= 1");
+  if (n > QRB_MAX_N) return set_error(QRB_ERR_UNSUPPORTED, "n exceeds QRB_MAX_N");
+  if (batch > (int64_t)1 << 31) return set_error(QRB_ERR_UNSUPPORTED, "batch exceeds 2^31");
   if (batch == 0) return QRB_OK;
-  if (n > qrb::kSmallMaxN && (size_t)batch * kTBytes > kNoAllocScratchBytes) return QRB_ERR_UNSUPPORTED;
-  if (A == nullptr || H == nullptr || tau == nullptr) return QRB_ERR_INVALID_ARG;
+  // Compared by division so that no product can wrap.
+  if (n > qrb::kSmallMaxN && batch > (int64_t)(kNoAllocScratchBytes / kTBytes))
+    return set_error(QRB_ERR_UNSUPPORTED,
+                     "batch exceeds the 2048 matrices the static scratch holds for n > 64");
+  if (A == nullptr || H == nullptr || tau == nullptr)
+    return set_error(QRB_ERR_INVALID_ARG, "A, H and tau must not be null");
   if ((reinterpret_cast<uintptr_t>(A) & 15u) || (reinterpret_cast<uintptr_t>(H) & 15u) ||
       (reinterpret_cast<uintptr_t>(tau) & 3u))
-    return QRB_ERR_INVALID_ARG;
+    return set_error(QRB_ERR_INVALID_ARG, "A and H must be 16-byte aligned, tau 4-byte aligned");
   int dev = 0, major = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
-    return QRB_ERR_CUDA;
-  if (major != 10) return QRB_ERR_DEVICE;
+    return set_error(QRB_ERR_CUDA, "could not query the current device");
+  if (major != 10) return set_error(QRB_ERR_DEVICE, "the current device is not sm_100");
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (n <= qrb::kSmallMaxN)
-    return qrb::launch_small(A, H, tau, nullptr, batch, n, 1, s) == cudaSuccess ? QRB_OK : QRB_ERR_CUDA;
+    return qrb::launch_small(A, H, tau, nullptr, batch, n, 1, s) == cudaSuccess
+               ? QRB_OK
+               : set_error(QRB_ERR_CUDA, "small-n kernel launch failed");
 
   void* scratch = nullptr;
-  if (scratch_address(&scratch) != cudaSuccess) return QRB_ERR_CUDA;
+  if (scratch_address(&scratch) != cudaSuccess)
+    return set_error(QRB_ERR_CUDA, "cudaGetSymbolAddress of the scratch array failed");
   float* T = static_cast<float*>(scratch);
   // Same right-looking blocked algorithm as qrb_geqrf_f32, with one T slot reused
   // by every panel (stream order keeps panel p+1 from overwriting it early).
   for (int k = 0; k < n; k += qrb::kNB) {
     const int b = n - k < qrb::kNB ? n - k : qrb::kNB;
     const float* src = k == 0 ? A : H;
-    if (qrb::launch_panel(src, H, tau, T, batch, n, k, b, s) != cudaSuccess) return QRB_ERR_CUDA;
+    if (qrb::launch_panel(src, H, tau, T, batch, n, k, b, s) != cudaSuccess)
+      return set_error(QRB_ERR_CUDA, "panel kernel launch failed");
     if (k + b < n &&
         qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, nullptr, s) != cudaSuccess)
-      return QRB_ERR_CUDA;
+      return set_error(QRB_ERR_CUDA, "trailing update launch failed");
   }
   return QRB_OK;
 }

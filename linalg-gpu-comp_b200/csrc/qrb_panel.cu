@@ -215,6 +215,9 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
 template <int RPT, int CL, int W = 8>
 cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int64_t batch,
                            int n, int k, int b, cudaStream_t s) {
+  const double m = n - k;
+  LaunchTimer timer("panel_kernel", s, (double)batch * (8.0 * m * b + 4.0 * b + 4096.0),
+                    (double)batch * 4.0 * m * b * b);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(batch * CL));
   cfg.blockDim = dim3(W * 32);

@@ -430,6 +430,10 @@ tiny_qr_kernel(const float* __restrict__ A, float* __restrict__ H, float* __rest
 cudaError_t launch_small(const float* A, float* H, float* tau, float* Q,
                          int64_t batch, int n, int mode, cudaStream_t s) {
   if (batch == 0) return cudaSuccess;
+  const double nn = (double)n * n;
+  const double bytes = (double)batch * (((mode & 1) ? 8 * nn : 4 * nn) + ((mode & 2) ? 4 * nn : 0) + 4.0 * n);
+  const double flops = (double)batch * (((mode & 1) ? 4.0 / 3 : 0) + ((mode & 2) ? 4.0 / 3 : 0)) * nn * n;
+  LaunchTimer timer(n <= 32 ? "tiny_qr_kernel" : "small_qr_kernel", s, bytes, flops);
   if (n <= 32) {
     const unsigned grid = (unsigned)((batch + kTinyWarps - 1) / kTinyWarps);
     tiny_qr_kernel<<<grid, kTinyWarps * 32, 0, s>>>(A, H, tau, Q, batch, n, mode);

@@ -32,6 +32,8 @@ SIGNATURES = {
     "qrb_orgqr_f32": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_qr_f32": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_geqrf_f32_noalloc": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp]),
+    "qrb_kernel_timing": (None, [ctypes.c_int]),
+    "qrb_kernel_timing_report": (_c_size, [ctypes.c_char_p, _c_size]),
     "qrb_host_workspace_size": (_c_size, [_c_int64, ctypes.c_int, ctypes.c_int]),
     "qrb_qr_f32_host": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
 }
@@ -76,3 +78,16 @@ def check(status: int) -> None:
     if status != QRB_OK:
         _, msg = last_error()
         raise QRBError(status, msg or lib().qrb_status_string(status).decode())
+
+
+def kernel_timing_report() -> dict:
+    """Per-kernel totals logged since the last report while ``qrb_kernel_timing(1)`` was on:
+    ``{name: {"launches", "ms", "bytes", "flops"}}`` (CUDA-event durations)."""
+    need = lib().qrb_kernel_timing_report(None, 0)
+    buf = ctypes.create_string_buffer(int(need) + 64)
+    lib().qrb_kernel_timing_report(buf, len(buf))
+    out = {}
+    for line in buf.value.decode().splitlines():
+        name, cnt, ms, by, fl = line.split()
+        out[name] = {"launches": int(cnt), "ms": float(ms), "bytes": float(by), "flops": float(fl)}
+    return out

@@ -28,7 +28,8 @@ def test_header_declares_the_api():
     assert set(declared_symbols()) == {
         "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
         "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error",
-        "qrb_host_workspace_size", "qrb_qr_f32_host", "qrb_kernel_launches"}
+        "qrb_host_workspace_size", "qrb_qr_f32_host", "qrb_kernel_launches", "qrb_kernel_timing",
+        "qrb_kernel_timing_report"}
 
 
 def test_library_exports_every_declared_symbol(lib):

@@ -73,3 +73,13 @@ def test_noalloc_rejects_batch_beyond_scratch(lib):
     st = lib.qrb_geqrf_f32_noalloc(A.data_ptr(), A.data_ptr(), A.data_ptr(), 2049, 128,
                                    torch.cuda.current_stream().cuda_stream)
     assert st == 2
+    # Batches whose T scratch size would wrap a 64-bit product, and batches beyond the
+    # 2^31 cap the other entry points enforce (n <= 64 too), are rejected the same way
+    # and leave a message in qrb_last_error.
+    for batch, n in ((1 << 62, 128), ((1 << 31) + 1, 32), ((1 << 31) + 1, 128)):
+        st = lib.qrb_geqrf_f32_noalloc(A.data_ptr(), A.data_ptr(), A.data_ptr(), batch, n,
+                                       torch.cuda.current_stream().cuda_stream)
+        assert st == 2, (batch, n)
+        buf = ctypes.create_string_buffer(256)
+        assert lib.qrb_last_error(buf, len(buf)) == 2
+        assert b"batch" in buf.value
