@@ -85,10 +85,18 @@ QRB_API int qrb_qr_f32(const float* A, float* H, float* tau, float* Q, int64_t b
 
 /* Returns, and clears, the first error code that a library kernel recorded on the
  * current device when one of its bounded waits on tensor-core or bulk-copy completion
- * ran out (0 = none).  Such a kernel skips the rest of its work and exits, so its
- * output is invalid.  Synchronises with the device.  No counterpart in the reference
+ * ran out (0 = none).  Such a kernel stops issuing copies, MMAs and stores, waits
+ * (bounded) for the ones it already has in flight, releases its tensor memory and
+ * exits, so its output is invalid.  Synchronises with the device.  No counterpart in the reference
  * (its kernels have no device-side waits). */
 QRB_API int qrb_device_error(void);
+
+/* Test hook for the device-side bounded waits: launches one CTA on `stream` whose two
+ * roles wait on mbarriers that nothing arrives on, with no copy or MMA in flight.  The
+ * first wait runs out after `limit` polls (1 .. 2^20), records error code 90 (read it
+ * with qrb_device_error) and stops the CTA, the other role's wait gives up at once, and
+ * the kernel exits.  Returns a qrb_status.  No counterpart in the reference. */
+QRB_API int qrb_selftest_bounded_wait(unsigned limit, void* stream);
 
 /* Number of kernels one qrb_qr_f32 (with_q != 0) or qrb_geqrf_f32 (with_q == 0) call
  * enqueues for (batch, n): 1 for n <= 64, otherwise one panel per 32 columns plus two or
@@ -102,7 +110,8 @@ QRB_API int64_t qrb_kernel_launches(int64_t batch, int n, int with_q);
  * waits for the logged events, writes one line per kernel name,
  *   "<name> <launches> <total ms> <algorithmic bytes> <flops>\n",
  * into buf (NUL-terminated, truncated to len), clears the log and returns the length
- * the full report needs (including the NUL).  For profilers and benchmarks; no
+ * the full report needs (including the NUL).  With buf == NULL it only returns that
+ * length and keeps the log.  For profilers and benchmarks; no
  * counterpart in the reference (its bench scripts time whole calls). */
 QRB_API void qrb_kernel_timing(int enable);
 QRB_API size_t qrb_kernel_timing_report(char* buf, size_t len);

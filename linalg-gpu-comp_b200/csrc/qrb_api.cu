@@ -11,7 +11,13 @@
 //              over the same T factors, with the identity generated on the fly.
 // Workspace: the T factors of every panel, [panel][batch][32][32] fp32, then the
 // tensor-core update's scratch (see ws_bytes).
+//
+// Large n (n % 4 == 0, n >= kWideMinN) takes the wide-block path instead: panels of 32
+// are grouped into blocks of 128 columns; inside a block each panel updates only the
+// rest of the block (column-limited 32-wide update), and the block as a whole updates
+// the trailing matrix and forms Q with 128-wide block reflectors (qrb_wide.cu).
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -58,18 +64,44 @@ size_t t_bytes(int64_t batch, int n) {
   return (size_t)n_panels(n) * (size_t)batch * qrb::kNB * qrb::kNB * sizeof(float);
 }
 
+// Sizes the workspace for the wide path whenever n qualifies (a pure size rule, so the
+// answer does not depend on the device); dispatch additionally needs TMA support.
+bool wide_eligible(int n) { return n % 4 == 0 && n >= qrb::kWideMinN; }
+
+// Smallest n dispatched to the wide path: kWideDefaultN, or the environment variable
+// QRB_WIDE_MIN_N (read once per process; values below kWideMinN are raised to it).
+int wide_min_n() {
+  static const int v = [] {
+    const char* e = std::getenv("QRB_WIDE_MIN_N");
+    int x = e != nullptr ? std::atoi(e) : qrb::kWideDefaultN;
+    return x < qrb::kWideMinN ? qrb::kWideMinN : x;
+  }();
+  return v;
+}
+
+bool use_wide(int n) { return wide_eligible(n) && n >= wide_min_n() && qrb::wide_supported(n); }
+
+size_t al256(size_t x) { return (x + 255) & ~size_t(255); }
+
 // Workspace: the T factors of every panel, then (for the tensor-core path, n % 4 == 0)
-// the update's scratch: W2 and the row-chunk partials of W^T (qrb::tc_ws_floats).
+// the update's scratch: W2 and the row-chunk partials of W^T (qrb::tc_ws_floats), then
+// (wide path) the block T factors, V and W2 pieces and Y partials (qrb::wide_ws_floats).
 size_t ws_bytes(int64_t batch, int n) {
   if (n <= qrb::kSmallMaxN) return 0;
   size_t bytes = t_bytes(batch, n);
-  if (n % 4 == 0) bytes = ((bytes + 255) & ~size_t(255)) + qrb::tc_ws_floats(batch, n) * sizeof(float);
+  if (n % 4 == 0) bytes = al256(bytes) + qrb::tc_ws_floats(batch, n) * sizeof(float);
+  if (wide_eligible(n)) bytes = al256(bytes) + qrb::wide_ws_floats(batch, n) * sizeof(float);
   return bytes;
 }
 
 float* tc_ws(void* ws, int64_t batch, int n) {
   if (n % 4 != 0) return nullptr;
-  return reinterpret_cast<float*>(static_cast<char*>(ws) + ((t_bytes(batch, n) + 255) & ~size_t(255)));
+  return reinterpret_cast<float*>(static_cast<char*>(ws) + al256(t_bytes(batch, n)));
+}
+
+float* wide_ws(void* ws, int64_t batch, int n) {
+  return reinterpret_cast<float*>(static_cast<char*>(ws) + al256(al256(t_bytes(batch, n)) +
+                                                                 qrb::tc_ws_floats(batch, n) * sizeof(float)));
 }
 
 // The kernels are built for sm_100a only: refuse anything else up front rather
@@ -128,8 +160,42 @@ float* panel_T(void* ws, int64_t batch, int p) {
   return static_cast<float*>(ws) + (size_t)p * (size_t)batch * qrb::kNB * qrb::kNB;
 }
 
+// Wide path: blocks of up to 128 columns, four panels each.  `with_t`: keep every
+// block's T factor for a following Q formation.
+int wide_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, void* ws, bool with_t,
+               cudaStream_t s) {
+  float* tcw = tc_ws(ws, batch, n);
+  float* wws = wide_ws(ws, batch, n);
+  for (int K = 0; K < n; K += qrb::kWideNB) {
+    const int bw = n - K < qrb::kWideNB ? n - K : qrb::kWideNB;
+    for (int k = K; k < K + bw; k += qrb::kNB) {
+      const int b = n - k < qrb::kNB ? n - k : qrb::kNB;
+      const float* src = k == 0 ? A : H;
+      float* T = panel_T(ws, batch, k / qrb::kNB);
+      QRB_CUDA(qrb::launch_panel(src, H, tau, T, batch, n, k, b, s), "panel kernel launch");
+      if (k + b < K + bw)
+        QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, K + bw, 1, 0, tcw, s),
+                 "in-block update launch");
+    }
+    QRB_CUDA(qrb::wide_geqrf_block(K == 0 ? A : H, H, panel_T(ws, batch, K / qrb::kNB), wws, batch, n, K, bw,
+                                   with_t, true, s),
+             "wide block update launch");
+  }
+  return QRB_OK;
+}
+
+int wide_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  float* wws = wide_ws(ws, batch, n);
+  for (int K = (n - 1) / qrb::kWideNB * qrb::kWideNB; K >= 0; K -= qrb::kWideNB) {
+    const int bw = n - K < qrb::kWideNB ? n - K : qrb::kWideNB;
+    QRB_CUDA(qrb::wide_orgqr_block(H, Q, wws, batch, n, K, bw, s), "wide orgqr block launch");
+  }
+  return QRB_OK;
+}
+
 int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, void* ws,
                   cudaStream_t s) {
+  if (use_wide(n)) return wide_geqrf(A, H, tau, batch, n, ws, false, s);
   const int np = n_panels(n);
   for (int p = 0; p < np; ++p) {
     const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
@@ -137,15 +203,17 @@ int blocked_geqrf(const float* A, float* H, float* tau, int64_t batch, int n, vo
     float* T = panel_T(ws, batch, p);
     QRB_CUDA(qrb::launch_panel(src, H, tau, T, batch, n, k, b, s), "panel kernel launch");
     if (k + b < n)
-      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, tc_ws(ws, batch, n), s), "trailing update launch");
+      QRB_CUDA(qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, n, 1, 0, tc_ws(ws, batch, n), s),
+               "trailing update launch");
   }
   return QRB_OK;
 }
 
 int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  if (use_wide(n)) return wide_orgqr(H, Q, batch, n, ws, s);
   for (int p = n_panels(n) - 1; p >= 0; --p) {
     const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
-    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, 0, 1, tc_ws(ws, batch, n), s),
+    QRB_CUDA(qrb::launch_apply(H, panel_T(ws, batch, p), Q, Q, batch, n, k, b, k, n, 0, 1, tc_ws(ws, batch, n), s),
              "orgqr block launch");
   }
   return QRB_OK;
@@ -157,6 +225,10 @@ int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
     QRB_CUDA(qrb::launch_small(A, H, tau, Q, batch, n, Q != nullptr ? 3 : 1, s), "small-n kernel launch");
     return QRB_OK;
   }
+  if (use_wide(n)) {
+    QRB_TRY(wide_geqrf(A, H, tau, batch, n, ws, Q != nullptr, s));
+    return Q != nullptr ? wide_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
+  }
   QRB_TRY(blocked_geqrf(A, H, tau, batch, n, ws, s));
   return Q != nullptr ? blocked_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
 }
@@ -165,14 +237,29 @@ int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n,
 int64_t count_launches(int64_t batch, int n, bool with_q) {
   if (n <= qrb::kSmallMaxN) return 1;
   const int np = n_panels(n);
-  auto update = [&](int k, int c0) -> int64_t {
-    return n % 4 == 0 ? qrb::tc_update_launches(batch, n, k, c0) : 1;
+  auto update = [&](int k, int c0, int c1) -> int64_t {
+    return n % 4 == 0 ? qrb::tc_update_launches(batch, n, k, c0, c1) : 1;
   };
+  if (use_wide(n)) {
+    int64_t total = 0;
+    for (int K = 0; K < n; K += qrb::kWideNB) {
+      const int bw = n - K < qrb::kWideNB ? n - K : qrb::kWideNB;
+      for (int k = K; k < K + bw; k += qrb::kNB) {
+        const int b = n - k < qrb::kNB ? n - k : qrb::kNB;
+        total += 1;
+        if (k + b < K + bw) total += update(k, k + b, K + bw);
+      }
+      const bool upd = K + bw < n;
+      total += qrb::wide_block_launches(batch, n, K, upd, upd || with_q, false);
+      if (with_q) total += qrb::wide_block_launches(batch, n, K, false, false, true);
+    }
+    return total;
+  }
   int64_t total = np;
   for (int p = 0; p < np; ++p) {
     const int k = p * qrb::kNB, b = n - k < qrb::kNB ? n - k : qrb::kNB;
-    if (k + b < n) total += update(k, k + b);
-    if (with_q) total += update(k, k);
+    if (k + b < n) total += update(k, k + b, n);
+    if (with_q) total += update(k, k, n);
   }
   return total;
 }
@@ -373,6 +460,15 @@ int qrb_orgqr_f32(const float* H, const float* tau, float* Q, int64_t batch, int
     return QRB_OK;
   }
   QRB_CUDA(qrb::launch_larft(H, tau, static_cast<float*>(workspace), batch, n, s), "larft launch");
+  if (use_wide(n)) {
+    float* wws = wide_ws(workspace, batch, n);
+    for (int K = 0; K < n; K += qrb::kWideNB) {
+      const int bw = n - K < qrb::kWideNB ? n - K : qrb::kWideNB;
+      QRB_CUDA(qrb::wide_geqrf_block(H, const_cast<float*>(H), panel_T(workspace, batch, K / qrb::kNB), wws, batch,
+                                     n, K, bw, true, false, s),
+               "wide T factor launch");
+    }
+  }
   return blocked_orgqr(H, Q, batch, n, workspace, s);
 }
 

@@ -1,4 +1,4 @@
-// Block reflector application  C[k:, c0:] -= V op(T) (V^T C[k:, c0:])  (SIMT fp32).
+// Block reflector application  C[k:, c0:c1] -= V op(T) (V^T C[k:, c0:c1])  (SIMT fp32).
 // Used for n % 4 != 0, where TMA cannot describe the rows; other n take the
 // tensor-core kernel in qrb_apply_tc.cu.
 //
@@ -50,11 +50,11 @@ __device__ __forceinline__ float cload(const float* __restrict__ src, size_t mof
 
 __global__ void __launch_bounds__(kThreads)
 apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const float* src,
-             float* C, int n, int k, int b, int c0, int trans_t, int ident) {
+             float* C, int n, int k, int b, int c0, int c1, int trans_t, int ident) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   ApplySmem& sm = *reinterpret_cast<ApplySmem*>(smem_raw);
   const int tid = threadIdx.x;
-  const int nstrips = (n - c0 + kTN - 1) / kTN;
+  const int nstrips = (c1 - c0 + kTN - 1) / kTN;
   const int64_t mat = blockIdx.x / nstrips;
   const int cs = c0 + (int)(blockIdx.x % nstrips) * kTN;   // first column of the strip
   const int m = n - k;
@@ -87,7 +87,7 @@ apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const fl
     }
     for (int idx = tid; idx < kRC1 * kTN; idx += kThreads) {
       int r = idx / kTN, c = idx % kTN;
-      sm.Cs[r][c] = (r0 + r < m) ? cload(src, moff, n, k + r0 + r, cs + c, kb, ident) : 0.f;
+      sm.Cs[r][c] = (r0 + r < m && cs + c < c1) ? cload(src, moff, n, k + r0 + r, cs + c, kb, ident) : 0.f;
     }
     __syncthreads();
 #pragma unroll 2
@@ -169,7 +169,7 @@ apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const fl
 #pragma unroll
       for (int y = 0; y < 4; ++y) {
         const int Cc = cs + tc + y;
-        if (Cc < n) C[moff + (size_t)R * n + Cc] = cload(src, moff, n, R, Cc, kb, ident) - o[x][y];
+        if (Cc < c1) C[moff + (size_t)R * n + Cc] = cload(src, moff, n, R, Cc, kb, ident) - o[x][y];
       }
     }
   }
@@ -178,18 +178,18 @@ apply_kernel(const float* __restrict__ H, const float* __restrict__ Tg, const fl
 }  // namespace
 
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
-                         int64_t batch, int n, int k, int b, int c0, int trans_t,
+                         int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                          int identity_fill, float* tcws, cudaStream_t s) {
-  if (batch == 0 || c0 >= n) return cudaSuccess;
+  if (batch == 0 || c0 >= c1) return cudaSuccess;
   if (tcws != nullptr && apply_tc_supported(n))
-    return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, tcws, s);
-  return launch_apply_simt(H, T, src, C, batch, n, k, b, c0, trans_t, identity_fill, s);
+    return launch_apply_tc(H, T, src, C, batch, n, k, b, c0, c1, trans_t, identity_fill, tcws, s);
+  return launch_apply_simt(H, T, src, C, batch, n, k, b, c0, c1, trans_t, identity_fill, s);
 }
 
 cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, float* C,
-                              int64_t batch, int n, int k, int b, int c0, int trans_t,
+                              int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                               int identity_fill, cudaStream_t s) {
-  if (batch == 0 || c0 >= n) return cudaSuccess;
+  if (batch == 0 || c0 >= c1) return cudaSuccess;
   const size_t smem = sizeof(ApplySmem);
   // The opt-in shared-memory limit is a per-device function attribute; set it once per device.
   static std::atomic<unsigned long long> attr_done{0};
@@ -202,11 +202,11 @@ cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, 
     if (e != cudaSuccess) return e;
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
-  dim3 grid((unsigned)((int64_t)((n - c0 + kTN - 1) / kTN) * batch));
-  const double m = n - k, nc = n - c0;
+  dim3 grid((unsigned)((int64_t)((c1 - c0 + kTN - 1) / kTN) * batch));
+  const double m = n - k, nc = c1 - c0;
   LaunchTimer timer("apply_kernel", s, (double)batch * (8.0 * m * nc + 4.0 * m * b),
                     (double)batch * 4.0 * m * nc * b);
-  apply_kernel<<<grid, kThreads, smem, s>>>(H, T, src, C, n, k, b, c0, trans_t, identity_fill);
+  apply_kernel<<<grid, kThreads, smem, s>>>(H, T, src, C, n, k, b, c0, c1, trans_t, identity_fill);
   return cudaGetLastError();
 }
 

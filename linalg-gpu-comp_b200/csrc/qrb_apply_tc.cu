@@ -24,7 +24,9 @@
 //                  tile, M=128 N=64 K=32 MMAs into double-buffered TMEM, the
 //                  epilogue subtracts from the TMA-loaded C tile and TMA-stores it.
 // Every mbarrier wait is bounded; a wait that runs out records an error code in
-// g_qrb_device_error and the kernel carries on to its TMEM release and exit.
+// g_qrb_device_error and stops the CTA: no further TMA, MMA or stores are issued, the
+// CTA waits (bounded) for the copies and MMAs it already has in flight, releases its
+// tensor memory and exits without writing results.
 // Requires n % 4 == 0 (TMA row strides are multiples of 16 bytes) and the workspace
 // of tc_ws_floats floats; launch_apply falls back to the SIMT kernel otherwise.
 #include <cudaTypedefs.h>
@@ -66,8 +68,16 @@ __device__ __constant__ int kTermB[kTerms] = {0, 1, 0};
 
 __device__ __forceinline__ void record_error(int code) { atomicCAS(&g_qrb_device_error, 0, code); }
 
-__device__ __forceinline__ void wait_or_flag(uint64_t* bar, uint32_t parity, int code) {
-  if (!mbar_wait(bar, parity)) record_error(code);
+// Bounded wait of one thread; false (with the code recorded) when it ran out.
+__device__ __forceinline__ bool wait_or_flag(uint64_t* bar, uint32_t parity, int code) {
+  if (mbar_wait(bar, parity)) return true;
+  record_error(code);
+  return false;
+}
+
+// Bounded wait inside a warp-specialised CTA (gives up when another role already did).
+__device__ __forceinline__ bool wait_role(uint64_t* bar, uint32_t parity, volatile int* abort, int code) {
+  return mbar_wait_abort(bar, parity, abort, &g_qrb_device_error, code);
 }
 
 // V[r][j] of the unit lower trapezoidal block (r relative to the panel top).
@@ -92,10 +102,6 @@ __device__ __forceinline__ void split4_store(unsigned char* p0, uint32_t pstride
   *reinterpret_cast<float4*>(p0 + pstride + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
 }
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
 constexpr int kMaxSplit = 8;            // row chunks of the W^T reduction
 constexpr uint32_t kWBox = kTN * 128;   // W2 piece box: 64 strip columns x 32 floats
 
@@ -104,7 +110,7 @@ constexpr uint32_t kWBox = kTN * 128;   // W2 piece box: 64 strip columns x 32 f
 // trapezoid here) and is split with C.  With a single row chunk (nsplit == 1) the CTA
 // holds the whole W^T of its strip and finishes W2 = op(T) W itself (the work of
 // w2_kernel, same arithmetic order), so the update needs no second launch.
-constexpr uint32_t kSmemA = 2 * kStage1 + 64 + 1024;
+constexpr uint32_t kSmemA = 2 * kStage1 + 64 + 1024;   // stages, 5 mbarriers + TMEM slot, alignment
 
 template <bool IDENT>
 __global__ void __launch_bounds__(kThreads, 3)
@@ -116,7 +122,8 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
                                                        ~uintptr_t(1023));
   uint64_t* tma1 = reinterpret_cast<uint64_t*>(sm + 2 * kStage1);
   uint64_t* mma1 = tma1 + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma1 + 2);
+  uint64_t* drain = mma1 + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(drain + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x % nsplit;
@@ -140,6 +147,7 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
     mbar_init(&tma1[1], 1);
     mbar_init(&mma1[0], 1);
     mbar_init(&mma1[1], 1);
+    mbar_init(drain, 1);
     fence_mbar_init();
     prefetch_tensormap(&map_src32);
     prefetch_tensormap(&map_hv32);
@@ -150,7 +158,10 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
+  // Stage loads armed but not yet waited on by the CTA (for the drain after an abort).
+  int armed_hi = -1;
   auto issue_stage = [&](int s) {
+    armed_hi = s;
     unsigned char* st = sm + (s & 1) * kStage1;
     const int y = r0 + s * kR1;
     mbar_arrive_expect_tx(&tma1[s & 1], 3 * kBox1);
@@ -167,20 +178,28 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
   float wacc[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) wacc[j] = 0.f;
-  auto gather_stage = [&](int s) {
-    wait_or_flag(&mma1[s & 1], (s >> 1) & 1, 13);
+  // Every decision to stop is made CTA-wide (__syncthreads_or), so all threads leave the
+  // stage loop at the same iteration and no barrier is left waiting.
+  auto gather_stage = [&](int s) -> bool {
+    if (!wait_or_flag(&mma1[s & 1], (s >> 1) & 1, 13)) return false;
     tc_fence_after();
     float p[32];
     tmem_ld32(tmem + tm_lane + (s & 1) * 32, p);
 #pragma unroll
     for (int j = 0; j < 32; ++j) wacc[j] += p[j];
     tc_fence_before();
+    return true;
   };
+  bool aborted = false, issued = false, issue_fail = false;
   for (int s = 0; s < nst; ++s) {
     const int buf = s & 1;
     const uint32_t par = (s >> 1) & 1;
     unsigned char* st = sm + buf * kStage1;
-    wait_or_flag(&tma1[buf], par, 11);
+    const bool landed = wait_or_flag(&tma1[buf], par, 11);
+    if (__syncthreads_or(!landed || issue_fail)) {
+      aborted = true;
+      break;
+    }
     for (int u = tid; u < 2 * kR1 * 8; u += kThreads) {
       const int box = u >> 8, r = (u >> 3) & 31, q = u & 7;
       const uint32_t off = off32b(r, q);
@@ -230,17 +249,31 @@ wpart_kernel(const __grid_constant__ CUtensorMap map_src32, const __grid_constan
         }
       }
       mma_commit(&mma1[buf]);
+      issued = true;
     }
-    if (s > 0) gather_stage(s - 1);
-    __syncthreads();
+    const bool gathered = s > 0 ? gather_stage(s - 1) : true;
+    if (__syncthreads_or(!gathered)) {
+      aborted = true;
+      break;
+    }
     if (tid == 0 && s + 2 < nst) {
-      wait_or_flag(&mma1[buf], par, 12);
-      issue_stage(s + 2);
+      if (wait_or_flag(&mma1[buf], par, 12)) issue_stage(s + 2);
+      else issue_fail = true;   // seen by every thread at the next stage's decision
     }
   }
-  gather_stage(nst - 1);
-  // M = 64 accumulator: lanes 0-15 of warp w hold W^T rows 16w + lane.
-  if (nsplit == 1) {
+  if (!aborted) aborted = __syncthreads_or(!gather_stage(nst - 1));
+  if (aborted) {
+    // Let this CTA's own copies and MMAs finish before its shared and tensor memory go.
+    if (tid == 0) {
+      for (int s = armed_hi - 1 < 0 ? 0 : armed_hi - 1; s <= armed_hi; ++s)
+        mbar_wait(&tma1[s & 1], (s >> 1) & 1, 1u << 22);
+      if (issued) {
+        mma_commit(drain);
+        mbar_wait(drain, 0, 1u << 22);
+      }
+    }
+  } else if (nsplit == 1) {
+    // M = 64 accumulator: lanes 0-15 of warp w hold W^T rows 16w + lane.
     // Every MMA has completed (gathered), so the stage buffers are free.
     __syncthreads();
     float(*Ws)[33] = reinterpret_cast<float(*)[33]>(sm);                   // Ws[i][j] = W^T[i][j]
@@ -362,11 +395,13 @@ constexpr uint32_t kSlotC = kPieces * kWBox;                // then C: 2 boxes x
 constexpr uint32_t kSlotBytes = kSlotC + 2 * kBox3;         // 48 KB
 constexpr uint32_t kOffBSlots = kPieces * kBox3;            // 32 KB
 constexpr uint32_t kOffBBar = kOffBSlots + kSlotsB * kSlotBytes;
-constexpr uint32_t kSmemB = kOffBBar + 160 + 1024;
+constexpr uint32_t kSmemB = kOffBBar + 256 + 1024;
 
 struct BarsB {
-  uint64_t full[kSlotsB], empty[kSlotsB], w2ready[kSlotsB], vfull, vready, vempty, accf[2], acce[2];
+  uint64_t full[kSlotsB], empty[kSlotsB], w2ready[kSlotsB], cdone[kSlotsB], vfull, vready, vempty, accf[2], acce[2],
+      drain;
   uint32_t tmem;
+  int abort;
 };
 
 struct ItemB {
@@ -388,7 +423,7 @@ template <bool IDENT>
 __global__ void __launch_bounds__(kThreadsB, 1)
 update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_constant__ CUtensorMap map_h128,
               const __grid_constant__ CUtensorMap map_hv128, const __grid_constant__ CUtensorMap map_w,
-              int64_t batch, int n, int k, int b, int c0, int nstrips, int ntiles, int ngroups, int gsize,
+              int64_t batch, int n, int k, int b, int c0, int c1, int nstrips, int ntiles, int ngroups, int gsize,
               int store_to_h) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -403,7 +438,10 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
       mbar_init(&bars.full[i], 1);
       mbar_init(&bars.empty[i], 1);
       mbar_init(&bars.w2ready[i], 4);
+      mbar_init(&bars.cdone[i], 4);
     }
+    mbar_init(&bars.drain, 1);
+    bars.abort = 0;
     mbar_init(&bars.vfull, 1);
     mbar_init(&bars.vready, 4);
     mbar_init(&bars.vempty, 1);
@@ -418,6 +456,7 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars.tmem;
+  volatile int* abort = &bars.abort;
 
   if (warp == 0) {
     // ---------------- producer ----------------
@@ -425,22 +464,35 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
       prefetch_tensormap(&map_src128);
       prefetch_tensormap(&map_w);
       prefetch_tensormap(&map_hv128);
-      int gs = 0, iter = 0;
-      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+      int gs = 0, iter = 0, v_last = -1;
+      int last_use[kSlotsB] = {-1, -1, -1, -1};
+      bool stop = false;
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
         const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
-        if (iter > 0) wait_or_flag(&bars.vempty, (iter - 1) & 1, 20);   // last MMA of the previous item
+        // last MMA of the previous item
+        if (iter > 0 && !wait_role(&bars.vempty, (iter - 1) & 1, abort, 20)) break;
         mbar_arrive_expect_tx(&bars.vfull, kBox3);
         tma_load_3d(sm + kOffBV, &map_hv128, k, it.y0, it.mat, &bars.vfull);
+        v_last = iter;
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kSlotsB, use = gs / kSlotsB;
-          if (use > 0) wait_or_flag(&bars.empty[slot], (use - 1) & 1, 21);
+          if (use > 0 && !wait_role(&bars.empty[slot], (use - 1) & 1, abort, 21)) {
+            stop = true;
+            break;
+          }
           unsigned char* sl = sm + kOffBSlots + slot * kSlotBytes;
           const int cs = c0 + s * kTN;
           mbar_arrive_expect_tx(&bars.full[slot], kWBox + 2 * kBox3);
           tma_load_3d(sl + kSlotW, &map_w, 0, cs, it.mat, &bars.full[slot]);
           tma_load_3d(sl + kSlotC, &map_src128, cs, it.y0, it.mat, &bars.full[slot]);
           tma_load_3d(sl + kSlotC + kBox3, &map_src128, cs + 32, it.y0, it.mat, &bars.full[slot]);
+          last_use[slot] = use;
         }
+      }
+      if (*abort) {   // let this CTA's loads land before its shared memory goes away
+        if (v_last >= 0) mbar_wait(&bars.vfull, v_last & 1, 1u << 22);
+        for (int sl = 0; sl < kSlotsB; ++sl)
+          if (last_use[sl] >= 0) mbar_wait(&bars.full[sl], last_use[sl] & 1, 1u << 22);
       }
     }
   } else if (warp == 1) {
@@ -449,13 +501,17 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
       constexpr uint32_t idesc3 = idesc_tf32(kR3, kTN, 0, 0);
       const uint32_t vb = smem_u32(sm + kOffBV);
       int gs = 0, iter = 0;
-      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+      bool issued = false, stop = false;
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
         const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
-        wait_or_flag(&bars.vready, iter & 1, 22);
+        if (!wait_role(&bars.vready, iter & 1, abort, 22)) break;
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kSlotsB, acc = gs & 1;
-          wait_or_flag(&bars.w2ready[slot], (gs / kSlotsB) & 1, 23);
-          if (gs >= 2) wait_or_flag(&bars.acce[acc], ((gs >> 1) - 1) & 1, 24);
+          if (!wait_role(&bars.w2ready[slot], (gs / kSlotsB) & 1, abort, 23) ||
+              (gs >= 2 && !wait_role(&bars.acce[acc], ((gs >> 1) - 1) & 1, abort, 24))) {
+            stop = true;
+            break;
+          }
           tc_fence_after();
           const uint32_t wb = smem_u32(sm + kOffBSlots + slot * kSlotBytes + kSlotW);
           const uint32_t d = tmem + acc * kTN;
@@ -469,17 +525,23 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
             }
           }
           mma_commit(&bars.accf[acc]);
+          issued = true;
         }
-        mma_commit(&bars.vempty);   // V of this item no longer read once these complete
+        if (!stop) mma_commit(&bars.vempty);   // V of this item no longer read once these complete
+      }
+      if (*abort && issued) {   // tensor memory must not be released under running MMAs
+        mma_commit(&bars.drain);
+        mbar_wait(&bars.drain, 0, 1u << 22);
       }
     }
   } else if (warp >= 6) {
     // ---------------- converters (warps 6-9) ----------------
     const int ct = tid - 192;   // 0..127
     int gs = 0, iter = 0;
-    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++iter) {
+    bool stop = false;
+    for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
       const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
-      wait_or_flag(&bars.vfull, iter & 1, 27);
+      if (!wait_role(&bars.vfull, iter & 1, abort, 27)) break;
       // V tile: 128 rows x 8 float4; rows relative to the panel top below 32 are masked.
 #pragma unroll 2
       for (int i = 0; i < 8; ++i) {
@@ -502,7 +564,10 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
       if (lane == 0) mbar_arrive(&bars.vready);
       for (int s = it.s0; s < it.s1; ++s, ++gs) {
         const int slot = gs % kSlotsB;
-        wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 28);
+        if (!wait_role(&bars.full[slot], (gs / kSlotsB) & 1, abort, 28)) {
+          stop = true;
+          break;
+        }
         unsigned char* p0 = sm + kOffBSlots + slot * kSlotBytes + kSlotW;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {   // W2: 64 rows x 8 float4
@@ -522,15 +587,19 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
     const CUtensorMap* map_store = store_to_h ? &map_h128 : &map_src128;
     const bool leader = (warp == 2 && lane == 0);
     int gs = 0;
-    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x) {
+    bool stop = false;
+    for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
       const ItemB it = item_b(item, k, ntiles, ngroups, gsize, nstrips);
       const int R = it.y0 + r;
       for (int s = it.s0; s < it.s1; ++s, ++gs) {
         const int slot = gs % kSlotsB, acc = gs & 1;
         const int cs = c0 + s * kTN;
         unsigned char* cbox = sm + kOffBSlots + slot * kSlotBytes + kSlotC;
-        wait_or_flag(&bars.full[slot], (gs / kSlotsB) & 1, 25);
-        wait_or_flag(&bars.accf[acc], (gs >> 1) & 1, 26);
+        if (!wait_role(&bars.full[slot], (gs / kSlotsB) & 1, abort, 25) ||
+            !wait_role(&bars.accf[acc], (gs >> 1) & 1, abort, 26)) {
+          stop = true;
+          break;
+        }
         tc_fence_after();
         float d[2][32];
         tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * kTN, d[0]);
@@ -558,10 +627,16 @@ update_kernel(const __grid_constant__ CUtensorMap map_src128, const __grid_const
           }
         }
         fence_proxy_async();
-        named_bar_sync(1, 128);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.cdone[slot]);
         if (leader) {
+          // every epilogue warp has written its rows of the tile
+          if (!wait_role(&bars.cdone[slot], (gs / kSlotsB) & 1, abort, 29)) {
+            stop = true;
+            break;
+          }
           tma_store_3d(map_store, cbox, cs, it.y0, it.mat);
-          if (cs + 32 < n) tma_store_3d(map_store, cbox + kBox3, cs + 32, it.y0, it.mat);
+          if (cs + 32 < c1) tma_store_3d(map_store, cbox + kBox3, cs + 32, it.y0, it.mat);
           tma_store_commit();
           // The store of the previous strip has finished reading its slot: hand it back.
           asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
@@ -593,13 +668,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 3-D fp32 map {cols, rows, depth} with row pitch `cols` floats, 32-column boxes.
-bool make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t rows, uint64_t depth,
+// 3-D fp32 map {cols, rows, depth} with row pitch `pitch` floats (>= cols), 32-column boxes.
+bool make_map(CUtensorMap* map, const float* base, uint64_t cols, uint64_t pitch, uint64_t rows, uint64_t depth,
               int box_rows, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[3] = {cols, rows, depth};
-  cuuint64_t strides[2] = {cols * 4, cols * rows * 4};
+  cuuint64_t strides[2] = {pitch * 4, pitch * rows * 4};
   cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
@@ -627,9 +702,9 @@ struct SplitPlan {
   int nsplit, chunk;
 };
 
-SplitPlan split_plan(int64_t batch, int n, int k, int c0) {
+SplitPlan split_plan(int64_t batch, int n, int k, int c0, int c1) {
   const int m = n - k;
-  const int64_t units = (int64_t)((n - c0 + kTN - 1) / kTN) * batch;
+  const int64_t units = (int64_t)((c1 - c0 + kTN - 1) / kTN) * batch;
   // 24 = 4 resident CTAs per SM x 6 waves
   const int64_t target = 24 * (int64_t)sm_count();
   int nsplit = (int)((target + units - 1) / units);
@@ -644,7 +719,7 @@ SplitPlan split_plan(int64_t batch, int n, int k, int c0) {
 template <bool IDENT>
 cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const CUtensorMap& s128,
                          const CUtensorMap& h128, const CUtensorMap& v128, const CUtensorMap& w, const float* T,
-                         float* part, float* w2, int64_t batch, int n, int k, int b, int c0, int trans_t,
+                         float* part, float* w2, int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                          int store_to_h, cudaStream_t st) {
   static std::atomic<unsigned long long> attr_done{0};
   int dev = 0;
@@ -659,12 +734,12 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
     attr_done.fetch_or(bit, std::memory_order_acq_rel);
   }
   const int m = n - k;
-  const int nstrips = (n - c0 + kTN - 1) / kTN;
+  const int nstrips = (c1 - c0 + kTN - 1) / kTN;
   const int ntiles = (m + kR3 - 1) / kR3;
   const int64_t units = (int64_t)nstrips * batch;
-  const SplitPlan sp = split_plan(batch, n, k, c0);
+  const SplitPlan sp = split_plan(batch, n, k, c0, c1);
   const int nsplit = sp.nsplit, chunk = sp.chunk;
-  const double mm = m, nc = n - c0;
+  const double mm = m, nc = c1 - c0;
   {
     LaunchTimer timer("wpart_kernel", st, (double)batch * (4.0 * mm * nc + 4.0 * mm * b * nstrips),
                       (double)batch * 2.0 * mm * nc * b);
@@ -691,38 +766,60 @@ cudaError_t launch_split(const CUtensorMap& s32, const CUtensorMap& v32, const C
   const unsigned gridb = (unsigned)(items < sms ? items : sms);
   LaunchTimer timer("update_kernel", st, (double)batch * (8.0 * mm * nc + 4.0 * mm * b),
                     (double)batch * 2.0 * mm * nc * b);
-  update_kernel<IDENT><<<gridb, kThreadsB, kSmemB, st>>>(s128, h128, v128, w, batch, n, k, b, c0, nstrips, ntiles,
-                                                         ngroups, gsize, store_to_h);
+  update_kernel<IDENT><<<gridb, kThreadsB, kSmemB, st>>>(s128, h128, v128, w, batch, n, k, b, c0, c1, nstrips,
+                                                         ntiles, ngroups, gsize, store_to_h);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C, int64_t batch,
-                            int n, int k, int b, int c0, int trans_t, int identity_fill, float* tcws,
+                            int n, int k, int b, int c0, int c1, int trans_t, int identity_fill, float* tcws,
                             cudaStream_t s) {
-  if (batch == 0 || c0 >= n) return cudaSuccess;
+  if (batch == 0 || c0 >= c1) return cudaSuccess;
   if (tcws == nullptr) return cudaErrorInvalidValue;
   const int store_to_h = (C == H) ? 1 : 0;
   if (!store_to_h && C != src) return cudaErrorInvalidValue;   // C is either H or the source
   float* w2 = tcws;
   float* part = w2 + (size_t)batch * n * 32;
   // 32-row boxes feed MN-major operands (32-byte-atom swizzle); 128-row boxes are
-  // K-major operands and the epilogue tile (plain 128-byte swizzle).
+  // K-major operands and the epilogue tile (plain 128-byte swizzle).  The maps of C
+  // (source and store) end at column c1: loads beyond it read zeros and stores beyond
+  // it are dropped, so a column-limited update touches nothing right of c1.
   const CUtensorMapSwizzle sw1 = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B, sw3 = CU_TENSOR_MAP_SWIZZLE_128B;
   CUtensorMap m_s32, m_s128, m_v32, m_v128, m_h128, m_w;
-  if (!make_map(&m_s32, src, n, n, batch, kR1, sw1) || !make_map(&m_s128, src, n, n, batch, kR3, sw3) ||
-      !make_map(&m_h128, H, n, n, batch, kR3, sw3) || !make_map(&m_v32, H, n, n, batch, kR1, sw1) ||
-      !make_map(&m_v128, H, n, n, batch, kR3, sw3) || !make_map(&m_w, w2, 32, n, batch, kTN, sw3))
+  if (!make_map(&m_s32, src, c1, n, n, batch, kR1, sw1) || !make_map(&m_s128, src, c1, n, n, batch, kR3, sw3) ||
+      !make_map(&m_h128, H, c1, n, n, batch, kR3, sw3) || !make_map(&m_v32, H, n, n, n, batch, kR1, sw1) ||
+      !make_map(&m_v128, H, n, n, n, batch, kR3, sw3) || !make_map(&m_w, w2, 32, 32, n, batch, kTN, sw3))
     return cudaErrorInvalidValue;
   return identity_fill ? launch_split<true>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
-                                            b, c0, trans_t, store_to_h, s)
+                                            b, c0, c1, trans_t, store_to_h, s)
                        : launch_split<false>(m_s32, m_v32, m_s128, m_h128, m_v128, m_w, T, part, w2, batch, n, k,
-                                             b, c0, trans_t, store_to_h, s);
+                                             b, c0, c1, trans_t, store_to_h, s);
 }
 
-int tc_update_launches(int64_t batch, int n, int k, int c0) {
-  return split_plan(batch, n, k, c0).nsplit > 1 ? 3 : 2;
+int tc_update_launches(int64_t batch, int n, int k, int c0, int c1) {
+  return split_plan(batch, n, k, c0, c1).nsplit > 1 ? 3 : 2;
+}
+
+int* device_error_flag() {
+  static std::atomic<int*> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (dev >= 0 && dev < 64) {
+    int* p = cache[dev].load(std::memory_order_acquire);
+    if (p != nullptr) return p;
+  }
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_qrb_device_error) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  if (dev >= 0 && dev < 64) cache[dev].store(static_cast<int*>(p), std::memory_order_release);
+  return static_cast<int*>(p);
 }
 
 int take_device_error() {

@@ -14,6 +14,12 @@ constexpr int kNB = 32;
 // entirely on chip.
 constexpr int kSmallMaxN = 64;
 
+// Wide blocks (qrb_wide.cu): for n % 4 == 0 and n >= kWideMinN the trailing update and
+// Q formation apply kWideNB reflectors at a time (four panels of kNB).
+constexpr int kWideNB = 128;
+constexpr int kWideMinN = 256;       // smallest n the workspace is sized for
+constexpr int kWideDefaultN = 256;   // smallest n dispatched there by default
+
 // Reflector convention of submissions/v1.py:9-38: |v0| below this is replaced by 1.
 constexpr float kEpsV0 = 1e-30f;
 
@@ -89,7 +95,7 @@ cudaError_t launch_small(const float* A, float* H, float* tau, float* Q,
 cudaError_t launch_panel(const float* src, float* H, float* tau, float* T,
                          int64_t batch, int n, int k, int b, cudaStream_t s);
 
-// Block reflector application  C[:, k:, c0:] -= V op(T) (V^T C[:, k:, c0:])
+// Block reflector application  C[:, k:, c0:c1] -= V op(T) (V^T C[:, k:, c0:c1])
 // with V = unit-lower reflectors H[:, k:, k:k+b].  trans_t = 1 applies T^T
 // (Q_k^T, the geqrf trailing update), 0 applies T (Q_k, orgqr).  `src` is read
 // (it may equal C).  If identity_fill, entries of C with row < k+b or column < k+b
@@ -98,24 +104,45 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T,
 // path (tf32 pieces of V and of W2, and the W^T partials); without it, or for
 // n % 4 != 0, the SIMT kernel runs.
 cudaError_t launch_apply(const float* H, const float* T, const float* src, float* C,
-                         int64_t batch, int n, int k, int b, int c0, int trans_t,
+                         int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                          int identity_fill, float* tcws, cudaStream_t s);
 size_t tc_ws_floats(int64_t batch, int n);
 
 // The two implementations launch_apply dispatches to (SIMT fp32 for any n).
 cudaError_t launch_apply_simt(const float* H, const float* T, const float* src, float* C,
-                              int64_t batch, int n, int k, int b, int c0, int trans_t,
+                              int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                               int identity_fill, cudaStream_t s);
 // Tensor-core (tcgen05, 3xTF32) variant of launch_apply; needs n % 4 == 0.
 bool apply_tc_supported(int n);
 cudaError_t launch_apply_tc(const float* H, const float* T, const float* src, float* C,
-                            int64_t batch, int n, int k, int b, int c0, int trans_t,
+                            int64_t batch, int n, int k, int b, int c0, int c1, int trans_t,
                             int identity_fill, float* tcws, cudaStream_t s);
 // Kernels one launch_apply_tc enqueues: wpart, w2 (only with a split W^T reduction), update.
-int tc_update_launches(int64_t batch, int n, int k, int c0);
+int tc_update_launches(int64_t batch, int n, int k, int c0, int c1);
+
+// ---- wide blocks (qrb_wide.cu) ----
+bool wide_supported(int n);
+// Workspace floats of the wide path (block T factors, V and W2 pieces, Y partials).
+size_t wide_ws_floats(int64_t batch, int n);
+// Kernels one wide block call enqueues.
+int wide_block_launches(int64_t batch, int n, int K, bool update, bool tfactor, bool orgqr);
+// geqrf, block at column K of width bw (its panels already factored, their T factors at
+// t32blk = [panel][batch][32][32]): forms the block's 128 x 128 T factor (want_t) and,
+// when `update`, applies the block to columns [K + bw, n) of H (read from src).
+cudaError_t wide_geqrf_block(const float* src, float* H, const float* t32blk, float* ws, int64_t batch, int n,
+                             int K, int bw, bool want_t, bool update, cudaStream_t s);
+// orgqr: Q[K:, K:] = (I - V T V^T) Q[K:, K:] with the identity generated where Q is not
+// formed yet, using the block T factor stored by wide_geqrf_block.
+cudaError_t wide_orgqr_block(const float* H, float* Q, float* ws, int64_t batch, int n, int K, int bw,
+                             cudaStream_t s);
 
 // First error code recorded by a kernel whose bounded wait ran out (0 = none); clears it.
 int take_device_error();
+// Device address of that error flag on the current device (looked up once per device).
+// Kernels outside the translation unit that defines the flag record through it: without
+// relocatable device code every translation unit is its own device module, so an
+// `extern __device__` declaration elsewhere would not name the same variable.
+int* device_error_flag();
 
 // T factors of all panels from (H, tau), for orgqr without a preceding geqrf.
 cudaError_t launch_larft(const float* H, const float* tau, float* T_all,

@@ -110,7 +110,7 @@ extern "C" QRB_API int qrb_geqrf_f32_noalloc(const float* A, float* H, float* ta
     if (qrb::launch_panel(src, H, tau, T, batch, n, k, b, s) != cudaSuccess)
       return set_error(QRB_ERR_CUDA, "panel kernel launch failed");
     if (k + b < n &&
-        qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, 1, 0, nullptr, s) != cudaSuccess)
+        qrb::launch_apply(H, T, src, H, batch, n, k, b, k + b, n, 1, 0, nullptr, s) != cudaSuccess)
       return set_error(QRB_ERR_CUDA, "trailing update launch failed");
   }
   return QRB_OK;

@@ -111,10 +111,13 @@ QRB_API void qrb_kernel_timing(int enable) { qrb::g_timing_on.store(enable != 0 
 QRB_API size_t qrb_kernel_timing_report(char* buf, size_t len) {
   using qrb::Record;
   auto& l = qrb::log_();
+  // A size query (buf == NULL) leaves the log in place; a report clears it.
+  const bool consume = buf != nullptr && len > 0;
   std::vector<Record> recs;
   {
     std::lock_guard<std::mutex> lock(l.mu);
-    recs.swap(l.recs);
+    if (consume) recs.swap(l.recs);
+    else recs = l.recs;
   }
   struct Agg {
     long long count = 0;
@@ -133,7 +136,7 @@ QRB_API size_t qrb_kernel_timing_report(char* buf, size_t len) {
     a.bytes += r.bytes;
     a.flops += r.flops;
   }
-  {
+  if (consume) {
     std::lock_guard<std::mutex> lock(l.mu);
     for (const Record& r : recs) {
       l.pool.push_back(r.e0);

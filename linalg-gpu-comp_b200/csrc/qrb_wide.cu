@@ -1,0 +1,1008 @@
+// Wide block reflectors for large n: the trailing update and Q formation applied
+// 128 reflectors at a time,
+//     C[K:, c0:] -= V op(T) (V^T C[K:, c0:]),   V = H[K:, K:K+128] (unit lower),
+// so that each trailing element is streamed through HBM once per 128 columns of the
+// factorisation instead of once per 32.  The reference gets its fat trailing GEMMs
+// the same way -- 256-wide blocks, geqrf panels and BF16x9 cublasLt products
+// (_qr_blocked, submission.py:838-894); here the block is factored as four 32-wide
+// panels (qrb_panel.cu) with narrow in-slab updates, and the block's products run on
+// the 5th-generation tensor cores in 3xTF32 (two tf32 pieces per operand, three
+// products, smallest first; see qrb_apply_tc.cu for the accuracy argument).
+//
+// Per block (K, width bw <= 128):
+//   vsplit_kernel   V (masked to the unit lower trapezoid) -> two tf32 pieces in HBM,
+//                   [batch][n][128] each, the B operand of ygemm_kernel.
+//   ygemm_kernel    Y[c][j] = sum_r C[r][c] V[r][j] for 128-column strips of C over a
+//                   chunk of rows: TMA stages of 32 rows, C split in shared memory,
+//                   M=128 N=128 K=8 MMAs into one TMEM accumulator per stage (double
+//                   buffered), stage partials summed in fp32 registers.  In geqrf the
+//                   first strip is the block itself masked to V, which gives the Gram
+//                   matrix V^T V of the block.
+//   tbuild_kernel   T (128 x 128) of the block from the four panel T factors and the
+//                   Gram matrix: T_ab = -T_aa sum_{a<c<=b} G_ac T_cb.
+//   w2build_kernel  W2[c][a] = sum_j op(T)[a][j] Y[c][j] in fp32, stored as two tf32
+//                   pieces [batch][n][128] (the K-major B operand of the update).
+//   wupdate_kernel  C -= V W2: persistent CTAs over (matrix, 128-row tile, strip
+//                   group); the tile's V pieces live in tensor memory (the MMA's A
+//                   operand), C strips of 32 columns (six-slot ring) and their W2
+//                   pieces (two-slot ring) stream in by TMA, M=128 N=32 K=8 MMAs into
+//                   four TMEM accumulators, the epilogue subtracts and TMA-stores.
+//
+// Every wait on another role of the CTA is bounded (mbar_wait_abort): a wait that runs
+// out records an error code in g_qrb_device_error and raises a CTA-wide abort flag;
+// every role then stops issuing work, the CTA waits (bounded) for its own TMA loads,
+// MMAs and stores in flight, releases its tensor memory and exits.  No TMA load uses
+// cluster multicast.
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "qrb_internal.cuh"
+#include "qrb_sm100.cuh"
+
+namespace qrb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kWB = kWideNB;   // reflectors per wide block
+
+// The three (A piece, B piece) products of 3xTF32, smallest first.
+__device__ __constant__ int kWTermA[3] = {1, 0, 0};
+__device__ __constant__ int kWTermB[3] = {0, 1, 0};
+
+__device__ __forceinline__ float vmask_w(float x, int r, int j, int bw) {
+  if (j >= bw) return 0.f;
+  return r > j ? x : (r == j ? 1.f : 0.f);
+}
+
+__device__ __forceinline__ uint32_t off32b_w(int r, int q) {   // 128B swizzle, 32-byte atoms
+  return r * 128u + (((((uint32_t)q >> 1) ^ (uint32_t)r) & 3u) << 5) + ((uint32_t)(q & 1) << 4);
+}
+__device__ __forceinline__ uint32_t off128_w(int r, int q) {   // 128B swizzle
+  return r * 128u + ((((uint32_t)q ^ (uint32_t)r) & 7u) << 4);
+}
+
+// `err` is the library's device error flag (device_error_flag()).
+__device__ __forceinline__ bool wwait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err, int code) {
+  return mbar_wait_abort(bar, parity, abort, err, code);
+}
+
+// ---- vsplit: V pieces of the block ------------------------------------------------------
+__global__ void __launch_bounds__(256)
+vsplit_kernel(const float* __restrict__ H, float* __restrict__ vp0, float* __restrict__ vp1, int n, int K,
+              int bw, int64_t units) {
+  const int m = n - K;
+  for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units;
+       u += (int64_t)gridDim.x * blockDim.x) {
+    const int q = (int)(u & 31);
+    const int64_t t = u >> 5;
+    const int r = (int)(t % m);
+    const int64_t mat = t / m;
+    const int j0 = 4 * q;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    if (j0 < bw) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(H + ((size_t)mat * n + K + r) * n + K + j0));
+      a[0] = v.x;
+      a[1] = v.y;
+      a[2] = v.z;
+      a[3] = v.w;
+    }
+    float x0[4], x1[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) split2_tf32(vmask_w(a[e], r, j0 + e, bw), x0[e], x1[e]);
+    const size_t o = ((size_t)mat * n + K + r) * kWB + j0;
+    *reinterpret_cast<float4*>(vp0 + o) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+    *reinterpret_cast<float4*>(vp1 + o) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+  }
+}
+
+// ---- ygemm: Y = C^T V over a row chunk, per 128-column strip ---------------------------
+constexpr int kYStages = 3;
+constexpr uint32_t kYBox = 32 * 128;          // 32 rows x 32 fp32
+constexpr uint32_t kYPiece = 4 * kYBox;       // 32 rows x 128 columns
+constexpr uint32_t kYStage = 4 * kYPiece;     // C pieces 0, 1, then V pieces 0, 1
+constexpr uint32_t kYOffV = 2 * kYPiece;
+constexpr uint32_t kYBarOff = kYStages * kYStage;
+constexpr uint32_t kSmemY = kYBarOff + 256 + 1024;
+constexpr int kYThreads = 320;   // producer, MMA, 4 converter warps, 4 gather warps
+
+struct YBars {
+  uint64_t full[kYStages], split[kYStages], sfree[kYStages], accf[2], acce[2], drain;
+  uint32_t tmem;
+  int abort;
+};
+
+// MODE 0 (geqrf): strip 0 is the block itself, read from H and masked to V (the Gram
+// matrix); other strips read `src`.  MODE 1 (orgqr): entries with row or column below
+// K + bw are the identity (Q not yet formed there).
+template <int MODE>
+__global__ void __launch_bounds__(kYThreads, 1)
+ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_h,
+             const __grid_constant__ CUtensorMap map_v0, const __grid_constant__ CUtensorMap map_v1,
+             float* __restrict__ ypart, int64_t batch, int n, int K, int bw, int nstrips, int chunk, int nsplit,
+             int ncolsY, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  YBars& bars = *reinterpret_cast<YBars*>(sm + kYBarOff);
+  volatile int* abort = &bars.abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x % nsplit;
+  const int t = blockIdx.x / nsplit;
+  const int strip = t % nstrips;
+  const int mat = t / nstrips;
+  const int cs = K + strip * kWB;
+  const int r0 = K + split * chunk;
+  const int r1 = min(n, r0 + chunk);
+  const int nst = (r1 - r0 + 31) / 32;
+  const int kb = K + bw;
+  const bool gram = (MODE == 0 && strip == 0);
+
+  if (tid == 0) {
+    for (int i = 0; i < kYStages; ++i) {
+      mbar_init(&bars.full[i], 1);
+      mbar_init(&bars.split[i], 4);
+      mbar_init(&bars.sfree[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bars.accf[i], 1);
+      mbar_init(&bars.acce[i], 4);
+    }
+    mbar_init(&bars.drain, 1);
+    bars.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars.tmem, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      const CUtensorMap* cmap = gram ? &map_h : &map_c;
+      prefetch_tensormap(cmap);
+      prefetch_tensormap(&map_v0);
+      prefetch_tensormap(&map_v1);
+      int last_use[kYStages] = {-1, -1, -1};
+      for (int s = 0; s < nst; ++s) {
+        const int st = s % kYStages, use = s / kYStages;
+        if (use > 0 && !wwait(&bars.sfree[st], (use - 1) & 1, abort, err, 31)) break;
+        unsigned char* sb = sm + st * kYStage;
+        const int y = r0 + s * 32;
+        mbar_arrive_expect_tx(&bars.full[st], kYPiece + 2 * kYPiece);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tma_load_3d(sb + j * kYBox, cmap, cs + 32 * j, y, mat, &bars.full[st]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          tma_load_3d(sb + kYOffV + j * kYBox, &map_v0, 32 * j, y, mat, &bars.full[st]);
+          tma_load_3d(sb + kYOffV + kYPiece + j * kYBox, &map_v1, 32 * j, y, mat, &bars.full[st]);
+        }
+        last_use[st] = use;
+      }
+      if (*abort) {   // let every load this CTA issued land before its shared memory goes away
+        for (int st = 0; st < kYStages; ++st)
+          if (last_use[st] >= 0) mbar_wait(&bars.full[st], last_use[st] & 1, 1u << 22);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, 128, 1, 1);
+      bool issued = false;
+      for (int s = 0; s < nst; ++s) {
+        const int st = s % kYStages, acc = s & 1;
+        if (!wwait(&bars.split[st], (s / kYStages) & 1, abort, err, 32)) break;
+        if (s >= 2 && !wwait(&bars.acce[acc], ((s >> 1) - 1) & 1, abort, err, 33)) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(sm + st * kYStage);
+        const uint32_t d = tmem + acc * 128;
+#pragma unroll
+        for (int tt = 0; tt < 3; ++tt) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t ad = sdesc_sw128_32b(base + kWTermA[tt] * kYPiece + kk * 1024, kYBox, 512);
+            const uint64_t bd = sdesc_sw128_32b(base + kYOffV + kWTermB[tt] * kYPiece + kk * 1024, kYBox, 512);
+            mma_tf32(d, ad, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&bars.accf[acc]);
+        mma_commit(&bars.sfree[st]);
+        issued = true;
+      }
+      if (*abort && issued) {   // tensor memory must not be released under running MMAs
+        mma_commit(&bars.drain);
+        mbar_wait(&bars.drain, 0, 1u << 22);
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------- converters: split the C stage into tf32 pieces ----------------
+    const int ct = tid - 64;
+    for (int s = 0; s < nst; ++s) {
+      const int st = s % kYStages;
+      if (!wwait(&bars.full[st], (s / kYStages) & 1, abort, err, 34)) break;
+      unsigned char* sb = sm + st * kYStage;
+      const int y = r0 + s * 32;
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i) {
+        const int u = ct + 128 * i;
+        const int box = u >> 8, r = (u >> 3) & 31, q = u & 7;
+        const uint32_t off = off32b_w(r, q);
+        unsigned char* p0 = sb + box * kYBox;
+        float4 v = *reinterpret_cast<float4*>(p0 + off);
+        float a[4] = {v.x, v.y, v.z, v.w};
+        const int R = y + r;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int Cc = cs + 32 * box + 4 * q + e;
+          if (MODE == 0) {
+            if (gram) a[e] = vmask_w(a[e], R - K, Cc - K, bw);
+          } else {
+            if (R < n && Cc < n && (R < kb || Cc < kb)) a[e] = R == Cc ? 1.f : 0.f;
+          }
+        }
+        float x0[4], x1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split2_tf32(a[e], x0[e], x1[e]);
+        *reinterpret_cast<float4*>(p0 + off) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+        *reinterpret_cast<float4*>(p0 + kYPiece + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.split[st]);
+    }
+  } else {
+    // ---------------- gatherers: stage partials -> fp32 register sums ----------------
+    const int q = warp & 3;   // TMEM lanes 32q.. = strip columns 32q + lane
+    float y[128];
+#pragma unroll
+    for (int j = 0; j < 128; ++j) y[j] = 0.f;
+    bool ok = true;
+    for (int s = 0; s < nst; ++s) {
+      const int acc = s & 1;
+      if (!wwait(&bars.accf[acc], (s >> 1) & 1, abort, err, 35)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float p[32];
+        tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + acc * 128 + 32 * c, p);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) y[32 * c + j] += p[j];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars.acce[acc]);
+    }
+    if (ok && !*abort) {
+      const int i = 32 * q + lane;
+      float4* dst = reinterpret_cast<float4*>(
+          ypart + ((((size_t)split * batch + mat) * ncolsY) + (cs - K) + i) * kWB);
+#pragma unroll
+      for (int c = 0; c < 32; ++c) dst[c] = make_float4(y[4 * c], y[4 * c + 1], y[4 * c + 2], y[4 * c + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ---- tbuild: T of the wide block from the panel T factors and the Gram matrix -----------
+constexpr uint32_t kSmemT = (2 * 128 * 129 + 32 * 33) * 4;
+
+__global__ void __launch_bounds__(256)
+tbuild_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int ncolsY,
+              const float* __restrict__ t32, int np, float* __restrict__ t128) {
+  extern __shared__ float smw[];
+  float(*G)[129] = reinterpret_cast<float(*)[129]>(smw);
+  float(*X)[129] = reinterpret_cast<float(*)[129]>(smw + 128 * 129);
+  float(*S)[33] = reinterpret_cast<float(*)[33]>(smw + 2 * 128 * 129);
+  const int tid = threadIdx.x;
+  const int64_t mat = blockIdx.x;
+  // Gram strip (summed over the row chunks) and the diagonal T blocks, 16 float4 per
+  // thread with all loads in flight before the shared-memory stores.
+  {
+    float4 g[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) g[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float4* src = reinterpret_cast<const float4*>(ypart + ((size_t)sp * batch + mat) * ncolsY * kWB);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const float4 v = __ldg(src + tid + 256 * k);
+        g[k].x += v.x;
+        g[k].y += v.y;
+        g[k].z += v.z;
+        g[k].w += v.w;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+      G[i][j] = g[k].x;
+      G[i][j + 1] = g[k].y;
+      G[i][j + 2] = g[k].z;
+      G[i][j + 3] = g[k].w;
+    }
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+      const int a = i >> 5, b = j >> 5;
+      float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (a == b && a < np)
+        t = __ldg(reinterpret_cast<const float4*>(t32 + ((size_t)a * batch + mat) * 1024 + (i & 31) * 32 + (j & 31)));
+      X[i][j] = t.x;
+      X[i][j + 1] = t.y;
+      X[i][j + 2] = t.z;
+      X[i][j + 3] = t.w;
+    }
+  }
+  __syncthreads();
+  const int ti = tid >> 3, tj = (tid & 7) * 4;
+  for (int b = 1; b < np; ++b) {
+    for (int a = b - 1; a >= 0; --a) {
+      // S = sum_{c=a+1..b} G_ac X_cb
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c = a + 1; c <= b; ++c) {
+#pragma unroll 8
+        for (int l = 0; l < 32; ++l) {
+          const float g = G[32 * a + ti][32 * c + l];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s[e] = fmaf(g, X[32 * c + l][32 * b + tj + e], s[e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S[ti][tj + e] = s[e];
+      __syncthreads();
+      // X_ab = -T_aa S
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+      for (int l = 0; l < 32; ++l) {
+        const float x = X[32 * a + ti][32 * a + l];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[e] = fmaf(x, S[l][tj + e], o[e]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) X[32 * a + ti][32 * b + tj + e] = -o[e];
+      __syncthreads();
+    }
+  }
+  float4* T = reinterpret_cast<float4*>(t128 + (size_t)mat * kWB * kWB);
+#pragma unroll 4
+  for (int k = 0; k < 16; ++k) {
+    const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+    T[u] = make_float4(X[i][j], X[i][j + 1], X[i][j + 2], X[i][j + 3]);
+  }
+}
+
+// ---- w2build: W2 = Y op(T)^T as two tf32 pieces ---------------------------------------------
+constexpr int kW2Cols = 64;
+constexpr uint32_t kSmemW2 = (128 * 132 + 128 * (kW2Cols + 4)) * 4;
+
+__global__ void __launch_bounds__(256)
+w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int ncolsY, int n, int K, int cfirst,
+               int ngroups, const float* __restrict__ t128, float* __restrict__ w2p0, float* __restrict__ w2p1,
+               int trans_t) {
+  extern __shared__ float smw[];
+  float(*Ot)[132] = reinterpret_cast<float(*)[132]>(smw);                     // Ot[j][a] = op(T)[a][j]
+  float(*Yt)[kW2Cols + 4] = reinterpret_cast<float(*)[kW2Cols + 4]>(smw + 128 * 132);   // Yt[j][i]
+  const int tid = threadIdx.x;
+  const int64_t mat = blockIdx.x / ngroups;
+  const int c0 = cfirst + (int)(blockIdx.x % ngroups) * kW2Cols;
+  // T (16 float4 per thread) and the Y strip (8 float4 per thread, summed over the row
+  // chunks), every load of a batch in flight before the shared-memory stores.
+  {
+    const float4* T4 = reinterpret_cast<const float4*>(t128 + (size_t)mat * kWB * kWB);
+    float4 t[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) t[k] = __ldg(T4 + tid + 256 * k);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int u = tid + 256 * k, r = u >> 5, c = 4 * (u & 31);
+      const float v[4] = {t[k].x, t[k].y, t[k].z, t[k].w};
+      if (trans_t) {   // op(T) = T^T: Ot[j][a] = T[j][a]
+        *reinterpret_cast<float4*>(&Ot[r][c]) = t[k];
+      } else {         // op(T) = T:   Ot[j][a] = T[a][j]
+#pragma unroll
+        for (int e = 0; e < 4; ++e) Ot[c + e][r] = v[e];
+      }
+    }
+    float4 y[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) y[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float* base = ypart + ((size_t)sp * batch + mat) * ncolsY * kWB;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+        if (c0 + i < n) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)(c0 + i - K) * kWB + j));
+          y[k].x += v.x;
+          y[k].y += v.y;
+          y[k].z += v.z;
+          y[k].w += v.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+      Yt[j][i] = y[k].x;
+      Yt[j + 1][i] = y[k].y;
+      Yt[j + 2][i] = y[k].z;
+      Yt[j + 3][i] = y[k].w;
+    }
+  }
+  __syncthreads();
+  const int i0 = 4 * (tid & 15), a0 = 8 * (tid >> 4);
+  // op(T) is lower triangular for geqrf (T^T: j <= a) and upper for orgqr (j >= a).
+  const int jlo = trans_t ? 0 : a0, jhi = trans_t ? a0 + 8 : 128;
+  float acc[4][8];
+#pragma unroll
+  for (int x = 0; x < 4; ++x)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[x][e] = 0.f;
+#pragma unroll 4
+  for (int j = jlo; j < jhi; ++j) {
+    const float4 yv = *reinterpret_cast<const float4*>(&Yt[j][i0]);
+    const float4 oa = *reinterpret_cast<const float4*>(&Ot[j][a0]);
+    const float4 ob = *reinterpret_cast<const float4*>(&Ot[j][a0 + 4]);
+    const float yy[4] = {yv.x, yv.y, yv.z, yv.w};
+    const float oo[8] = {oa.x, oa.y, oa.z, oa.w, ob.x, ob.y, ob.z, ob.w};
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[x][e] = fmaf(oo[e], yy[x], acc[x][e]);
+  }
+#pragma unroll
+  for (int x = 0; x < 4; ++x) {
+    const int c = c0 + i0 + x;
+    if (c >= n) continue;
+    float p0[8], p1[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split2_tf32(acc[x][e], p0[e], p1[e]);
+    float4* d0 = reinterpret_cast<float4*>(w2p0 + ((size_t)mat * n + c) * kWB + a0);
+    float4* d1 = reinterpret_cast<float4*>(w2p1 + ((size_t)mat * n + c) * kWB + a0);
+    d0[0] = make_float4(p0[0], p0[1], p0[2], p0[3]);
+    d0[1] = make_float4(p0[4], p0[5], p0[6], p0[7]);
+    d1[0] = make_float4(p1[0], p1[1], p1[2], p1[3]);
+    d1[1] = make_float4(p1[4], p1[5], p1[6], p1[7]);
+  }
+}
+
+// ---- wupdate: C -= V W2 with V in tensor memory -------------------------------------------------
+// Warp roles: 0 = C/V producer, 1 = MMA issuer (TMEM owner), 2-5 = epilogue (they also
+// split each item's V tile into the tensor memory), 6 = W2 producer.  C strips (the HBM
+// stream) and W2 pieces (re-read from L2 by every row tile) flow through separate rings,
+// so C loads run several strips ahead of the MMAs; four TMEM accumulators let the MMAs
+// run ahead of the epilogue.
+constexpr int kUCSlots = 6;
+constexpr int kUWSlots = 2;
+constexpr int kUAcc = 4;
+constexpr uint32_t kUVBox = 128 * 128;             // 128 rows x 32 fp32
+constexpr uint32_t kUOffW = 4 * kUVBox;            // V staging: the tile's 128 x 128 block
+constexpr uint32_t kUWBox = 32 * 128;              // 32 columns x 32 K values
+constexpr uint32_t kUWPiece = 4 * kUWBox;          // K = 128
+constexpr uint32_t kUWSlot = 2 * kUWPiece;         // two tf32 pieces
+constexpr uint32_t kUOffC = kUOffW + kUWSlots * kUWSlot;
+constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUVBox;
+constexpr uint32_t kSmemU = kUBarOff + 512 + 1024;
+constexpr int kUThreads = 224;
+constexpr int kUTN = 32;                           // strip width (N)
+
+struct UBars {
+  uint64_t cfull[kUCSlots], cempty[kUCSlots], cdone[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vfull, vempty,
+      vready, accf[kUAcc], acce[kUAcc], drain;
+  uint32_t tmem;
+  int abort;
+};
+static_assert(sizeof(UBars) <= 512, "barrier block");
+static_assert(kSmemU <= 232448, "shared memory");
+
+struct UItem {
+  int mat, y0, s0, s1;
+};
+
+__device__ __forceinline__ UItem u_item(int64_t item, int K, int ntiles, int ngroups, int gsize, int nstrips) {
+  UItem it;
+  const int g = (int)(item % ngroups);
+  const int64_t t = item / ngroups;
+  it.y0 = K + (int)(t % ntiles) * 128;
+  it.mat = (int)(t / ntiles);
+  it.s0 = g * gsize;
+  it.s1 = min(nstrips, it.s0 + gsize);
+  return it;
+}
+
+template <bool IDENT>
+__global__ void __launch_bounds__(kUThreads, 1)
+wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_src,
+               const __grid_constant__ CUtensorMap map_dst, const __grid_constant__ CUtensorMap map_w0,
+               const __grid_constant__ CUtensorMap map_w1, int64_t batch, int n, int K, int bw, int c0, int nstrips,
+               int ntiles, int ngroups, int gsize, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  UBars& bars = *reinterpret_cast<UBars*>(sm + kUBarOff);
+  volatile int* abort = &bars.abort;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int kb = K + bw;
+  const int64_t nitems = batch * ntiles * ngroups;
+
+  if (tid == 0) {
+    for (int i = 0; i < kUCSlots; ++i) {
+      mbar_init(&bars.cfull[i], 1);
+      mbar_init(&bars.cempty[i], 1);
+      mbar_init(&bars.cdone[i], 4);
+    }
+    for (int i = 0; i < kUWSlots; ++i) {
+      mbar_init(&bars.wfull[i], 1);
+      mbar_init(&bars.wempty[i], 1);
+    }
+    mbar_init(&bars.vfull, 1);
+    mbar_init(&bars.vempty, 4);
+    mbar_init(&bars.vready, 4);
+    for (int i = 0; i < kUAcc; ++i) {
+      mbar_init(&bars.accf[i], 1);
+      mbar_init(&bars.acce[i], 4);
+    }
+    mbar_init(&bars.drain, 1);
+    bars.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tmem_alloc(&bars.tmem, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bars.tmem;
+  constexpr uint32_t kAcc = 256;   // accumulators after the two V pieces (128 columns each)
+
+  if (warp == 0) {
+    // ---------------- C / V producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&map_v);
+      prefetch_tensormap(&map_src);
+      int gs = 0, iter = 0, v_last = -1;
+      int last_use[kUCSlots];
+#pragma unroll
+      for (int i = 0; i < kUCSlots; ++i) last_use[i] = -1;
+      bool stop = false;
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+        const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+        if (iter > 0 && !wwait(&bars.vempty, (iter - 1) & 1, abort, err, 41)) break;
+        mbar_arrive_expect_tx(&bars.vfull, 4 * kUVBox);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tma_load_3d(sm + j * kUVBox, &map_v, K + 32 * j, it.y0, it.mat, &bars.vfull);
+        v_last = iter;
+        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+          const int slot = gs % kUCSlots, use = gs / kUCSlots;
+          if (use > 0 && !wwait(&bars.cempty[slot], (use - 1) & 1, abort, err, 42)) {
+            stop = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&bars.cfull[slot], kUVBox);
+          tma_load_3d(sm + kUOffC + slot * kUVBox, &map_src, c0 + s * kUTN, it.y0, it.mat, &bars.cfull[slot]);
+          last_use[slot] = use;
+        }
+      }
+      if (*abort) {   // let every load this CTA issued land before its shared memory goes away
+        if (v_last >= 0) mbar_wait(&bars.vfull, v_last & 1, 1u << 22);
+        for (int sl = 0; sl < kUCSlots; ++sl)
+          if (last_use[sl] >= 0) mbar_wait(&bars.cfull[sl], last_use[sl] & 1, 1u << 22);
+      }
+    }
+  } else if (warp == 6) {
+    // ---------------- W2 producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(&map_w0);
+      prefetch_tensormap(&map_w1);
+      int gs = 0;
+      int last_use[kUWSlots] = {-1, -1};
+      bool stop = false;
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+        const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+          const int slot = gs % kUWSlots, use = gs / kUWSlots;
+          if (use > 0 && !wwait(&bars.wempty[slot], (use - 1) & 1, abort, err, 50)) {
+            stop = true;
+            break;
+          }
+          unsigned char* sl = sm + kUOffW + slot * kUWSlot;
+          const int cs = c0 + s * kUTN;
+          mbar_arrive_expect_tx(&bars.wfull[slot], kUWSlot);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            tma_load_3d(sl + j * kUWBox, &map_w0, 32 * j, cs, it.mat, &bars.wfull[slot]);
+            tma_load_3d(sl + kUWPiece + j * kUWBox, &map_w1, 32 * j, cs, it.mat, &bars.wfull[slot]);
+          }
+          last_use[slot] = use;
+        }
+      }
+      if (*abort) {
+        for (int sl = 0; sl < kUWSlots; ++sl)
+          if (last_use[sl] >= 0) mbar_wait(&bars.wfull[sl], last_use[sl] & 1, 1u << 22);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32(128, kUTN, 0, 0);
+      int gs = 0, iter = 0;
+      bool issued = false, stop = false;
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+        const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+        if (!wwait(&bars.vready, iter & 1, abort, err, 43)) break;
+        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+          const int slot = gs % kUWSlots, acc = gs % kUAcc;
+          if (!wwait(&bars.wfull[slot], (gs / kUWSlots) & 1, abort, err, 44) ||
+              (gs >= kUAcc && !wwait(&bars.acce[acc], ((gs / kUAcc) - 1) & 1, abort, err, 45))) {
+            stop = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t wb = smem_u32(sm + kUOffW + slot * kUWSlot);
+          const uint32_t d = tmem + kAcc + acc * kUTN;
+#pragma unroll
+          for (int tt = 0; tt < 3; ++tt) {
+#pragma unroll
+            for (int kk = 0; kk < 16; ++kk) {
+              const uint32_t a = tmem + kWTermA[tt] * 128 + kk * 8;
+              const uint64_t bd =
+                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);
+              mma_tf32_ta(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(&bars.accf[acc]);
+          mma_commit(&bars.wempty[slot]);
+          issued = true;
+        }
+      }
+      if (*abort && issued) {   // tensor memory must not be released under running MMAs
+        mma_commit(&bars.drain);
+        mbar_wait(&bars.drain, 0, 1u << 22);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps 2-5: V into tensor memory, then C -= V W2 ----------------
+    const int q = warp & 3;
+    const int r = 32 * q + lane;   // tile row = TMEM lane
+    const uint32_t tl = (uint32_t)(32 * q) << 16;
+    const bool leader = (warp == 2 && lane == 0);
+    int gs = 0, iter = 0;
+    bool stop = false;
+    for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+      const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+      const int R = it.y0 + r;
+      if (!wwait(&bars.vfull, iter & 1, abort, err, 46)) break;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        float x0[32], x1[32];
+        const unsigned char* box = sm + c * kUVBox;
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq) {
+          const float4 v = *reinterpret_cast<const float4*>(box + off128_w(r, qq));
+          const float a[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            split2_tf32(vmask_w(a[e], R - K, 32 * c + 4 * qq + e, bw), x0[4 * qq + e], x1[4 * qq + e]);
+        }
+        tmem_st32(tmem + tl + 32 * c, x0);
+        tmem_st32(tmem + tl + 128 + 32 * c, x1);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars.vready);
+        mbar_arrive(&bars.vempty);
+      }
+      for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        const int slot = gs % kUCSlots, acc = gs % kUAcc;
+        const int cs = c0 + s * kUTN;
+        unsigned char* cbox = sm + kUOffC + slot * kUVBox;
+        if (!wwait(&bars.cfull[slot], (gs / kUCSlots) & 1, abort, err, 47) ||
+            !wwait(&bars.accf[acc], (gs / kUAcc) & 1, abort, err, 48)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        float d[32];
+        tmem_ld32(tmem + tl + kAcc + acc * kUTN, d);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.acce[acc]);
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq) {
+          const uint32_t off = off128_w(r, qq);
+          const float4 cv4 = *reinterpret_cast<const float4*>(cbox + off);
+          float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if constexpr (IDENT) {
+              const int Cc = cs + 4 * qq + e;
+              if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+            }
+            cv[e] -= d[4 * qq + e];
+          }
+          *reinterpret_cast<float4*>(cbox + off) = make_float4(cv[0], cv[1], cv[2], cv[3]);
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bars.cdone[slot]);
+        if (leader) {
+          if (!wwait(&bars.cdone[slot], (gs / kUCSlots) & 1, abort, err, 49)) {
+            stop = true;
+            break;
+          }
+          tma_store_3d(&map_dst, cbox, cs, it.y0, it.mat);
+          tma_store_commit();
+          // The previous strip's store has finished reading its slot: hand the slot back.
+          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          if (gs > 0) mbar_arrive(&bars.cempty[(gs - 1) % kUCSlots]);
+        }
+      }
+    }
+    if (leader) tma_store_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_w() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 3-D fp32 map: `cols` x `rows` x `depth` with row pitch `pitch` floats; boxes of 32
+// columns x box_rows rows.
+bool wmap(CUtensorMap* map, const float* base, uint64_t cols, uint64_t pitch, uint64_t rows, uint64_t depth,
+          int box_rows, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn_w();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {cols, rows, depth};
+  cuuint64_t strides[2] = {pitch * 4, pitch * rows * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int nblocks(int n) { return (n + kWB - 1) / kWB; }
+int ycols(int n) { return nblocks(n) * kWB; }
+
+// Row chunks of the Y reduction: enough CTAs (one per SM) for about two waves, but
+// never chunks under 512 rows.
+struct YPlan {
+  int nstrips, nsplit, chunk;
+};
+
+YPlan y_plan(int64_t batch, int n, int K, int cend) {
+  YPlan p;
+  const int m = n - K;
+  p.nstrips = (cend - K + kWB - 1) / kWB;
+  const int64_t units = (int64_t)p.nstrips * (batch > 0 ? batch : 1);
+  const int64_t target = 2 * (int64_t)sm_count();
+  int ns = (int)((target + units - 1) / units);
+  const int max_split = (m + 511) / 512;
+  ns = ns < 1 ? 1 : (ns > max_split ? max_split : ns);
+  if (ns > 8) ns = 8;
+  int chunk = (m + ns - 1) / ns;
+  chunk = (chunk + 31) / 32 * 32;
+  p.chunk = chunk;
+  p.nsplit = (m + chunk - 1) / chunk;
+  return p;
+}
+
+struct WideWs {
+  float *t128, *vp0, *vp1, *w0, *w1, *ypart;
+};
+
+size_t al(size_t x) { return (x + 63) & ~size_t(63); }   // floats: keep 256-byte alignment
+
+WideWs carve(float* ws, int64_t batch, int n) {
+  WideWs w;
+  const size_t mat = (size_t)batch * n * kWB;
+  w.t128 = ws;
+  w.vp0 = w.t128 + al((size_t)nblocks(n) * batch * kWB * kWB);
+  w.vp1 = w.vp0 + al(mat);
+  w.w0 = w.vp1 + al(mat);
+  w.w1 = w.w0 + al(mat);
+  w.ypart = w.w1 + al(mat);
+  return w;
+}
+
+bool set_smem_attrs() {
+  static std::atomic<unsigned long long> done{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const unsigned long long bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return true;
+  if (cudaFuncSetAttribute(ygemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemY) != cudaSuccess ||
+      cudaFuncSetAttribute(ygemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemY) != cudaSuccess ||
+      cudaFuncSetAttribute(wupdate_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemU) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(wupdate_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemU) !=
+          cudaSuccess ||
+      cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemT) != cudaSuccess ||
+      cudaFuncSetAttribute(w2build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemW2) != cudaSuccess)
+    return false;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return true;
+}
+
+cudaError_t run_vsplit(const float* H, const WideWs& w, int64_t batch, int n, int K, int bw, cudaStream_t s) {
+  const int64_t units = batch * (int64_t)(n - K) * 32;
+  int64_t blocks = (units + 255) / 256;
+  const int64_t cap = 8 * (int64_t)sm_count();
+  if (blocks > cap) blocks = cap;
+  LaunchTimer timer("vsplit_kernel", s, (double)batch * (n - K) * (4.0 * bw + 8.0 * kWB));
+  vsplit_kernel<<<(unsigned)blocks, 256, 0, s>>>(H, w.vp0, w.vp1, n, K, bw, units);
+  return cudaGetLastError();
+}
+
+// Y over columns [K, cend) of `src` (MODE 0: strip 0 from H, masked to V).
+cudaError_t run_ygemm(int mode, const float* src, const float* H, const WideWs& w, int64_t batch, int n, int K,
+                      int bw, int cend, YPlan& plan, cudaStream_t s) {
+  plan = y_plan(batch, n, K, cend);
+  int* err = device_error_flag();
+  if (err == nullptr) return cudaErrorInvalidValue;
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B;
+  CUtensorMap mc, mh, mv0, mv1;
+  if (!wmap(&mc, src, n, n, n, batch, 32, sw) || !wmap(&mh, H, n, n, n, batch, 32, sw) ||
+      !wmap(&mv0, w.vp0, kWB, kWB, n, batch, 32, sw) || !wmap(&mv1, w.vp1, kWB, kWB, n, batch, 32, sw))
+    return cudaErrorInvalidValue;
+  const unsigned grid = (unsigned)((int64_t)plan.nstrips * batch * plan.nsplit);
+  const double m = n - K, nc = cend - K;
+  LaunchTimer timer("ygemm_kernel", s, (double)batch * (4.0 * m * nc + 8.0 * m * kWB * plan.nstrips),
+                    (double)batch * 2.0 * m * nc * kWB);
+  if (mode == 0)
+    ygemm_kernel<0><<<grid, kYThreads, kSmemY, s>>>(mc, mh, mv0, mv1, w.ypart, batch, n, K, bw, plan.nstrips,
+                                                      plan.chunk, plan.nsplit, ycols(n), err);
+  else
+    ygemm_kernel<1><<<grid, kYThreads, kSmemY, s>>>(mc, mh, mv0, mv1, w.ypart, batch, n, K, bw, plan.nstrips,
+                                                      plan.chunk, plan.nsplit, ycols(n), err);
+  return cudaGetLastError();
+}
+
+cudaError_t run_tbuild(const WideWs& w, const YPlan& plan, const float* t32blk, int np, int blk, int64_t batch,
+                       int n, cudaStream_t s) {
+  LaunchTimer timer("tbuild_kernel", s, (double)batch * (plan.nsplit + 1) * kWB * kWB * 4.0);
+  tbuild_kernel<<<(unsigned)batch, 256, kSmemT, s>>>(w.ypart, plan.nsplit, batch, ycols(n), t32blk, np,
+                                                    w.t128 + (size_t)blk * batch * kWB * kWB);
+  return cudaGetLastError();
+}
+
+cudaError_t run_w2build(const WideWs& w, const YPlan& plan, int blk, int64_t batch, int n, int K, int cfirst,
+                        int trans_t, cudaStream_t s) {
+  const int ngroups = (n - cfirst + kW2Cols - 1) / kW2Cols;
+  if (ngroups <= 0) return cudaSuccess;
+  const double nc = n - cfirst;
+  LaunchTimer timer("w2build_kernel", s, (double)batch * nc * kWB * 4.0 * (plan.nsplit + 2),
+                    (double)batch * nc * kWB * kWB);
+  w2build_kernel<<<(unsigned)(batch * ngroups), 256, kSmemW2, s>>>(
+      w.ypart, plan.nsplit, batch, ycols(n), n, K, cfirst, ngroups, w.t128 + (size_t)blk * batch * kWB * kWB, w.w0,
+      w.w1, trans_t);
+  return cudaGetLastError();
+}
+
+cudaError_t run_wupdate(bool ident, const float* H, const float* src, float* dst, const WideWs& w, int64_t batch,
+                        int n, int K, int bw, int c0, cudaStream_t s) {
+  int* err = device_error_flag();
+  if (err == nullptr) return cudaErrorInvalidValue;
+  CUtensorMap mv, msrc, mdst, mw0, mw1;
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!wmap(&mv, H, n, n, n, batch, 128, sw) || !wmap(&msrc, src, n, n, n, batch, 128, sw) ||
+      !wmap(&mdst, dst, n, n, n, batch, 128, sw) || !wmap(&mw0, w.w0, kWB, kWB, n, batch, 32, sw) ||
+      !wmap(&mw1, w.w1, kWB, kWB, n, batch, 32, sw))
+    return cudaErrorInvalidValue;
+  const int m = n - K;
+  const int nstrips = (n - c0 + kUTN - 1) / kUTN;
+  const int ntiles = (m + 127) / 128;
+  const int64_t tiles = batch * ntiles;
+  const int sms = sm_count();
+  int ngroups = (int)((4 * (int64_t)sms + tiles - 1) / tiles);
+  ngroups = ngroups < 1 ? 1 : (ngroups > nstrips ? nstrips : ngroups);
+  const int gsize = (nstrips + ngroups - 1) / ngroups;
+  ngroups = (nstrips + gsize - 1) / gsize;
+  const int64_t items = tiles * ngroups;
+  const unsigned grid = (unsigned)(items < sms ? items : sms);
+  const double mm = m, nc = n - c0;
+  LaunchTimer timer("wupdate_kernel", s, (double)batch * (8.0 * mm * nc + 4.0 * mm * kWB * ngroups),
+                    (double)batch * 2.0 * mm * nc * kWB);
+  if (ident)
+    wupdate_kernel<true><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, mdst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+                                                         ntiles, ngroups, gsize, err);
+  else
+    wupdate_kernel<false><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, mdst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+                                                          ntiles, ngroups, gsize, err);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+bool wide_supported(int n) { return n % 4 == 0 && n >= kWideMinN && encode_fn_w() != nullptr; }
+
+size_t wide_ws_floats(int64_t batch, int n) {
+  size_t ymax = 0;
+  for (int K = 0; K < n; K += kWB) {
+    const YPlan p = y_plan(batch, n, K, n);
+    const size_t y = (size_t)p.nsplit * batch * ycols(n) * kWB;
+    if (y > ymax) ymax = y;
+  }
+  const size_t mat = (size_t)batch * n * kWB;
+  return al((size_t)nblocks(n) * batch * kWB * kWB) + 4 * al(mat) + al(ymax);
+}
+
+int wide_block_launches(int64_t batch, int n, int K, bool update, bool tfactor, bool orgqr) {
+  (void)batch;
+  (void)K;
+  if (orgqr) return 4;   // vsplit, ygemm, w2build, wupdate
+  int c = 0;
+  if (update || tfactor) c += 2;   // vsplit, ygemm
+  if (tfactor) c += 1;             // tbuild
+  if (update) c += 2;              // w2build, wupdate
+  return c;
+}
+
+cudaError_t wide_geqrf_block(const float* src, float* H, const float* t32blk, float* ws, int64_t batch, int n,
+                             int K, int bw, bool want_t, bool update, cudaStream_t s) {
+  if (!set_smem_attrs()) return cudaErrorInvalidValue;
+  update = update && K + bw < n;
+  if (!update && !want_t) return cudaSuccess;
+  const WideWs w = carve(ws, batch, n);
+  const int blk = K / kWB;
+  cudaError_t e = run_vsplit(H, w, batch, n, K, bw, s);
+  if (e != cudaSuccess) return e;
+  YPlan plan;
+  e = run_ygemm(0, update ? src : H, H, w, batch, n, K, bw, update ? n : K + bw, plan, s);
+  if (e != cudaSuccess) return e;
+  if (want_t || update) {
+    // T is needed by the update as well (W2 = T^T Y).
+    e = run_tbuild(w, plan, t32blk, (bw + kNB - 1) / kNB, blk, batch, n, s);
+    if (e != cudaSuccess) return e;
+  }
+  if (!update) return cudaSuccess;
+  e = run_w2build(w, plan, blk, batch, n, K, K + bw, 1, s);
+  if (e != cudaSuccess) return e;
+  return run_wupdate(false, H, src, H, w, batch, n, K, bw, K + bw, s);
+}
+
+cudaError_t wide_orgqr_block(const float* H, float* Q, float* ws, int64_t batch, int n, int K, int bw,
+                             cudaStream_t s) {
+  if (!set_smem_attrs()) return cudaErrorInvalidValue;
+  const WideWs w = carve(ws, batch, n);
+  const int blk = K / kWB;
+  cudaError_t e = run_vsplit(H, w, batch, n, K, bw, s);
+  if (e != cudaSuccess) return e;
+  YPlan plan;
+  e = run_ygemm(1, Q, H, w, batch, n, K, bw, n, plan, s);
+  if (e != cudaSuccess) return e;
+  e = run_w2build(w, plan, blk, batch, n, K, K, 0, s);
+  if (e != cudaSuccess) return e;
+  return run_wupdate(true, H, Q, Q, w, batch, n, K, bw, K, s);
+}
+
+}  // namespace qrb

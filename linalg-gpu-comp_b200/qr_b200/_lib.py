@@ -33,6 +33,7 @@ SIGNATURES = {
     "qrb_qr_f32": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),
     "qrb_geqrf_f32_noalloc": (ctypes.c_int, [_fp, _fp, _fp, _c_int64, ctypes.c_int, _vp]),
     "qrb_kernel_timing": (None, [ctypes.c_int]),
+    "qrb_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint, _vp]),
     "qrb_kernel_timing_report": (_c_size, [ctypes.c_char_p, _c_size]),
     "qrb_host_workspace_size": (_c_size, [_c_int64, ctypes.c_int, ctypes.c_int]),
     "qrb_qr_f32_host": (ctypes.c_int, [_fp, _fp, _fp, _fp, _c_int64, ctypes.c_int, _vp, _c_size, _vp]),

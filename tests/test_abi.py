@@ -29,7 +29,7 @@ def test_header_declares_the_api():
         "qrb_version", "qrb_status_string", "qrb_last_error", "qrb_workspace_size",
         "qrb_geqrf_f32", "qrb_orgqr_f32", "qrb_qr_f32", "qrb_geqrf_f32_noalloc", "qrb_device_error",
         "qrb_host_workspace_size", "qrb_qr_f32_host", "qrb_kernel_launches", "qrb_kernel_timing",
-        "qrb_kernel_timing_report"}
+        "qrb_kernel_timing_report", "qrb_selftest_bounded_wait"}
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -46,15 +46,51 @@ def test_version_and_status_strings(lib):
     assert lib.qrb_status_string(99) == b"unknown status"
 
 
+def _wide_floats(batch, n, sms=148):
+    """Wide-path scratch (csrc/qrb_wide.cu wide_ws_floats): block T factors, two V and two
+    W2 piece arrays, and the Y partials of the largest row-chunk split."""
+    al = lambda x: (x + 63) // 64 * 64
+    nblk = (n + 127) // 128
+    ymax = 0
+    for K in range(0, n, 128):
+        m = n - K
+        nstrips = (n - K + 127) // 128
+        ns = max(1, min(-(-2 * sms // (nstrips * batch)), (m + 511) // 512, 8))
+        chunk = (-(-m // ns) + 31) // 32 * 32
+        ns = -(-m // chunk)
+        ymax = max(ymax, ns * batch * nblk * 128 * 128)
+    return al(nblk * batch * 128 * 128) + 4 * al(batch * n * 128) + al(ymax)
+
+
+def _ws(batch, n):
+    al = lambda x: (x + 255) // 256 * 256
+    t = -(-n // 32) * batch * 4096
+    if n <= 64:
+        return 0
+    b = t
+    if n % 4 == 0:
+        b = al(b) + (batch * n * 32 + 8 * batch * (-(-n // 64)) * 64 * 32) * 4
+    if n % 4 == 0 and n >= 256:
+        b = al(b) + _wide_floats(batch, n) * 4
+    return b
+
+
 @pytest.mark.parametrize("batch,n,expect", [
     (10, 1, 0), (10, 64, 0), (10, 65, 3 * 10 * 32 * 32 * 4),
     # T factors + (n % 4 == 0) W2 (fp32) + 8 row-chunk W^T partials
-    (7, 512, 16 * 7 * 4096 + (1 + 8) * 7 * 512 * 32 * 4),
-    (32, 2048, 64 * 32 * 4096 + (1 + 8) * 32 * 2048 * 32 * 4),
+    (7, 128, 4 * 7 * 4096 + (1 + 8) * 7 * 128 * 32 * 4),
     (3, 100, 4 * 3 * 4096 + (3 * 100 * 32 + 8 * 3 * 128 * 32) * 4),
+    # n >= 256, n % 4 == 0: plus the wide-block scratch
+    (7, 512, _ws(7, 512)), (32, 2048, _ws(32, 2048)), (2, 260, _ws(2, 260)), (2, 258, _ws(2, 258)),
     (1, 4097, 0), (-1, 100, 0)])
 def test_workspace_size(lib, batch, n, expect):
     assert lib.qrb_workspace_size(batch, n) == expect
+
+
+def test_wide_workspace_components():
+    # b32_n2048: 16 blocks of T (8 MiB each... 2 MiB per block at batch 32), V/W2 pieces 32 MiB each
+    assert _wide_floats(32, 2048) >= 16 * 32 * 128 * 128 + 4 * 32 * 2048 * 128
+    assert _ws(2, 258) == 9 * 2 * 4096          # n % 4 != 0: T factors only (SIMT update)
 
 
 def _err(lib):
