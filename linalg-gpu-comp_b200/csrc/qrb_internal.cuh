@@ -18,7 +18,8 @@ constexpr int kSmallMaxN = 64;
 // Q formation apply kWideNB reflectors at a time (four panels of kNB).
 constexpr int kWideNB = 128;
 constexpr int kWideMinN = 256;       // smallest n the workspace is sized for
-constexpr int kWideDefaultN = 256;   // smallest n dispatched there by default
+constexpr int kWideDefaultN = 512;   // smallest n dispatched there by default (measured: n = 256 and
+                                     // 352 are faster on the 32-wide path)
 
 // Reflector convention of submissions/v1.py:9-38: |v0| below this is replaced by 1.
 constexpr float kEpsV0 = 1e-30f;

@@ -121,7 +121,11 @@ __device__ __forceinline__ void tc_fence_before() {
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
 // 32 consecutive 32-bit TMEM columns of this thread's lane (warp w reads lanes 32*(w%4)..).
+// tcgen05.ld/st are warp-collective (.sync.aligned): every lane must execute them
+// together, so the wrappers reconverge the warp first (lanes leave an mbarrier spin loop
+// at different iterations, and a diverged warp reads or writes wrong lanes).
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  __syncwarp();
   uint32_t r[32];
   // The wait is in the same statement: the destination registers are undefined
   // until tcgen05.wait::ld completes, so nothing may read them in between.
@@ -144,6 +148,7 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // Stores 32 consecutive 32-bit TMEM columns of this thread's lane and waits for the
 // stores to complete (warp w writes lanes 32*(w%4)..).
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  __syncwarp();
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
       "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
@@ -162,7 +167,10 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       : "memory");
 }
 
-__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() {
+  __syncwarp();
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
 // ---- MMA -----------------------------------------------------------------------------
 // Instruction descriptor, kind::tf32 with fp32 accumulation.

@@ -24,9 +24,10 @@
 //                   pieces [batch][n][128] (the K-major B operand of the update).
 //   wupdate_kernel  C -= V W2: persistent CTAs over (matrix, 128-row tile, strip
 //                   group); the tile's V pieces live in tensor memory (the MMA's A
-//                   operand), C strips of 32 columns (six-slot ring) and their W2
-//                   pieces (two-slot ring) stream in by TMA, M=128 N=32 K=8 MMAs into
-//                   four TMEM accumulators, the epilogue subtracts and TMA-stores.
+//                   operand), C strips of 64 columns (three-slot ring) and their W2
+//                   pieces (two-slot ring) stream in by TMA, M=128 N=64 K=8 MMAs into
+//                   four TMEM accumulators; the epilogue subtracts and writes each
+//                   finished row to global memory directly.
 //
 // Every wait on another role of the CTA is bounded (mbar_wait_abort): a wait that runs
 // out records an error code in g_qrb_device_error and raises a CTA-wide abort flag;
@@ -415,6 +416,8 @@ w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int n
         for (int e = 0; e < 4; ++e) Ot[c + e][r] = v[e];
       }
     }
+    // Lane = column here (consecutive lanes store consecutive columns of a Yt row, so
+    // the transposing shared-memory stores do not conflict).
     float4 y[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) y[k] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -422,7 +425,7 @@ w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int n
       const float* base = ypart + ((size_t)sp * batch + mat) * ncolsY * kWB;
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+        const int u = tid + 256 * k, i = u & 63, j = 4 * (u >> 6);
         if (c0 + i < n) {
           const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)(c0 + i - K) * kWB + j));
           y[k].x += v.x;
@@ -434,7 +437,7 @@ w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int n
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
+      const int u = tid + 256 * k, i = u & 63, j = 4 * (u >> 6);
       Yt[j][i] = y[k].x;
       Yt[j + 1][i] = y[k].y;
       Yt[j + 2][i] = y[k].z;
@@ -479,28 +482,33 @@ w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int n
 }
 
 // ---- wupdate: C -= V W2 with V in tensor memory -------------------------------------------------
-// Warp roles: 0 = C/V producer, 1 = MMA issuer (TMEM owner), 2-5 = epilogue (they also
-// split each item's V tile into the tensor memory), 6 = W2 producer.  C strips (the HBM
-// stream) and W2 pieces (re-read from L2 by every row tile) flow through separate rings,
-// so C loads run several strips ahead of the MMAs; four TMEM accumulators let the MMAs
-// run ahead of the epilogue.
-constexpr int kUCSlots = 6;
+// Warp roles: 0 = C producer, 1 = MMA issuer (TMEM owner), 2-5 = epilogue (they also
+// load each item's V tile, one row per thread, and split it into the tensor memory),
+// 6 = W2 producer.  C strips (the HBM stream) and W2 pieces (re-read from L2 by every
+// row tile) flow through separate rings, so C loads run several strips ahead of the
+// MMAs and W2 loads several strips ahead of their L2 latency; four TMEM accumulators
+// let the MMAs run ahead of the epilogue.
+// Strips are 64 columns: a tf32 MMA costs at least ~44 cycles whatever its N (measured
+// on B200: M=128 N=32 K=8 44.6 cycles, N=64 ~46, N=128 64, N=256 128), so N=32 strips
+// would cap the kernel near 4.4 TB/s on the MMA issue alone.
+constexpr int kUCSlots = 3;
 constexpr int kUWSlots = 2;
 constexpr int kUAcc = 4;
-constexpr uint32_t kUVBox = 128 * 128;             // 128 rows x 32 fp32
-constexpr uint32_t kUOffW = 4 * kUVBox;            // V staging: the tile's 128 x 128 block
-constexpr uint32_t kUWBox = 32 * 128;              // 32 columns x 32 K values
+constexpr int kUTN = 64;                           // strip width (N)
+constexpr uint32_t kUCBox = 128 * 128;             // 128 rows x 32 fp32
+constexpr uint32_t kUCSlot = 2 * kUCBox;           // one C strip: 128 rows x 64 columns
+constexpr uint32_t kUOffW = 0;
+constexpr uint32_t kUWBox = kUTN * 128;            // 64 columns x 32 K values
 constexpr uint32_t kUWPiece = 4 * kUWBox;          // K = 128
 constexpr uint32_t kUWSlot = 2 * kUWPiece;         // two tf32 pieces
 constexpr uint32_t kUOffC = kUOffW + kUWSlots * kUWSlot;
-constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUVBox;
+constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUCSlot;
 constexpr uint32_t kSmemU = kUBarOff + 512 + 1024;
 constexpr int kUThreads = 224;
-constexpr int kUTN = 32;                           // strip width (N)
 
 struct UBars {
-  uint64_t cfull[kUCSlots], cempty[kUCSlots], cdone[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vfull, vempty,
-      vready, accf[kUAcc], acce[kUAcc], drain;
+  uint64_t cfull[kUCSlots], cempty[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vready,
+      accf[kUAcc], acce[kUAcc], drain;
   uint32_t tmem;
   int abort;
 };
@@ -524,8 +532,8 @@ __device__ __forceinline__ UItem u_item(int64_t item, int K, int ntiles, int ngr
 
 template <bool IDENT>
 __global__ void __launch_bounds__(kUThreads, 1)
-wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_src,
-               const __grid_constant__ CUtensorMap map_dst, const __grid_constant__ CUtensorMap map_w0,
+wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap map_src, float* dst,
+               const __grid_constant__ CUtensorMap map_w0,
                const __grid_constant__ CUtensorMap map_w1, int64_t batch, int n, int K, int bw, int c0, int nstrips,
                int ntiles, int ngroups, int gsize, int* err) {
   extern __shared__ unsigned char smem_raw[];
@@ -540,15 +548,12 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
   if (tid == 0) {
     for (int i = 0; i < kUCSlots; ++i) {
       mbar_init(&bars.cfull[i], 1);
-      mbar_init(&bars.cempty[i], 1);
-      mbar_init(&bars.cdone[i], 4);
+      mbar_init(&bars.cempty[i], 4);
     }
     for (int i = 0; i < kUWSlots; ++i) {
       mbar_init(&bars.wfull[i], 1);
       mbar_init(&bars.wempty[i], 1);
     }
-    mbar_init(&bars.vfull, 1);
-    mbar_init(&bars.vempty, 4);
     mbar_init(&bars.vready, 4);
     for (int i = 0; i < kUAcc; ++i) {
       mbar_init(&bars.accf[i], 1);
@@ -566,35 +571,30 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
   constexpr uint32_t kAcc = 256;   // accumulators after the two V pieces (128 columns each)
 
   if (warp == 0) {
-    // ---------------- C / V producer ----------------
+    // ---------------- C producer ----------------
     if (lane == 0) {
-      prefetch_tensormap(&map_v);
       prefetch_tensormap(&map_src);
-      int gs = 0, iter = 0, v_last = -1;
+      int gs = 0;
       int last_use[kUCSlots];
 #pragma unroll
       for (int i = 0; i < kUCSlots; ++i) last_use[i] = -1;
       bool stop = false;
-      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
-        if (iter > 0 && !wwait(&bars.vempty, (iter - 1) & 1, abort, err, 41)) break;
-        mbar_arrive_expect_tx(&bars.vfull, 4 * kUVBox);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) tma_load_3d(sm + j * kUVBox, &map_v, K + 32 * j, it.y0, it.mat, &bars.vfull);
-        v_last = iter;
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kUCSlots, use = gs / kUCSlots;
           if (use > 0 && !wwait(&bars.cempty[slot], (use - 1) & 1, abort, err, 42)) {
             stop = true;
             break;
           }
-          mbar_arrive_expect_tx(&bars.cfull[slot], kUVBox);
-          tma_load_3d(sm + kUOffC + slot * kUVBox, &map_src, c0 + s * kUTN, it.y0, it.mat, &bars.cfull[slot]);
+          mbar_arrive_expect_tx(&bars.cfull[slot], kUCSlot);
+          unsigned char* cb = sm + kUOffC + slot * kUCSlot;
+          tma_load_3d(cb, &map_src, c0 + s * kUTN, it.y0, it.mat, &bars.cfull[slot]);
+          tma_load_3d(cb + kUCBox, &map_src, c0 + s * kUTN + 32, it.y0, it.mat, &bars.cfull[slot]);
           last_use[slot] = use;
         }
       }
       if (*abort) {   // let every load this CTA issued land before its shared memory goes away
-        if (v_last >= 0) mbar_wait(&bars.vfull, v_last & 1, 1u << 22);
         for (int sl = 0; sl < kUCSlots; ++sl)
           if (last_use[sl] >= 0) mbar_wait(&bars.cfull[sl], last_use[sl] & 1, 1u << 22);
       }
@@ -605,7 +605,9 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       prefetch_tensormap(&map_w0);
       prefetch_tensormap(&map_w1);
       int gs = 0;
-      int last_use[kUWSlots] = {-1, -1};
+      int last_use[kUWSlots];
+#pragma unroll
+      for (int i = 0; i < kUWSlots; ++i) last_use[i] = -1;
       bool stop = false;
       for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
@@ -656,7 +658,7 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
             for (int kk = 0; kk < 16; ++kk) {
               const uint32_t a = tmem + kWTermA[tt] * 128 + kk * 8;
               const uint64_t bd =
-                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);
+                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);   // N = 64 rows
               mma_tf32_ta(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
             }
           }
@@ -675,20 +677,26 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
     const int q = warp & 3;
     const int r = 32 * q + lane;   // tile row = TMEM lane
     const uint32_t tl = (uint32_t)(32 * q) << 16;
-    const bool leader = (warp == 2 && lane == 0);
     int gs = 0, iter = 0;
     bool stop = false;
     for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
       const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
       const int R = it.y0 + r;
-      if (!wwait(&bars.vfull, iter & 1, abort, err, 46)) break;
+      if (*abort) break;
+      // V row R of the block (row R - K of the reflectors), masked to the unit lower
+      // trapezoid; rows past n are zero.  The MMAs of the previous item have completed
+      // (its last accumulator was read), so the tensor memory may be overwritten.
+      const float4* vrow = reinterpret_cast<const float4*>(H + ((size_t)it.mat * n + R) * n + K);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float x0[32], x1[32];
-        const unsigned char* box = sm + c * kUVBox;
+        float4 vv[8];
+#pragma unroll
+        for (int qq = 0; qq < 8; ++qq)
+          vv[qq] = (R < n && 32 * c + 4 * qq < bw) ? __ldg(vrow + 8 * c + qq) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
         for (int qq = 0; qq < 8; ++qq) {
-          const float4 v = *reinterpret_cast<const float4*>(box + off128_w(r, qq));
+          const float4 v = vv[qq];
           const float a[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e)
@@ -700,57 +708,58 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bars.vready);
-        mbar_arrive(&bars.vempty);
-      }
+      if (lane == 0) mbar_arrive(&bars.vready);
       for (int s = it.s0; s < it.s1; ++s, ++gs) {
         const int slot = gs % kUCSlots, acc = gs % kUAcc;
         const int cs = c0 + s * kUTN;
-        unsigned char* cbox = sm + kUOffC + slot * kUVBox;
+        unsigned char* cbox = sm + kUOffC + slot * kUCSlot;
         if (!wwait(&bars.cfull[slot], (gs / kUCSlots) & 1, abort, err, 47) ||
             !wwait(&bars.accf[acc], (gs / kUAcc) & 1, abort, err, 48)) {
           stop = true;
           break;
         }
         tc_fence_after();
-        float d[32];
-        tmem_ld32(tmem + tl + kAcc + acc * kUTN, d);
+        float d[2][32];
+        tmem_ld32(tmem + tl + kAcc + acc * kUTN, d[0]);
+        tmem_ld32(tmem + tl + kAcc + acc * kUTN + 32, d[1]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bars.acce[acc]);
+        // Row R of the strip: C - V W2, written straight to global memory (one 256-byte
+        // row per thread); no shared-memory write-back or bulk store is needed.
+        float4 out[16];
 #pragma unroll
-        for (int qq = 0; qq < 8; ++qq) {
-          const uint32_t off = off128_w(r, qq);
-          const float4 cv4 = *reinterpret_cast<const float4*>(cbox + off);
-          float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
+        for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            if constexpr (IDENT) {
-              const int Cc = cs + 4 * qq + e;
-              if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+          for (int qq = 0; qq < 8; ++qq) {
+            const float4 cv4 = *reinterpret_cast<const float4*>(cbox + h * kUCBox + off128_w(r, qq));
+            float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              if constexpr (IDENT) {
+                const int Cc = cs + 32 * h + 4 * qq + e;
+                if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+              }
+              cv[e] -= d[h][4 * qq + e];
             }
-            cv[e] -= d[4 * qq + e];
+            out[8 * h + qq] = make_float4(cv[0], cv[1], cv[2], cv[3]);
           }
-          *reinterpret_cast<float4*>(cbox + off) = make_float4(cv[0], cv[1], cv[2], cv[3]);
         }
+        if (R < n) {
+          float4* drow = reinterpret_cast<float4*>(dst + ((size_t)it.mat * n + R) * n + cs);
+#pragma unroll
+          for (int qq = 0; qq < 16; ++qq)
+            if (cs + 4 * qq < n) drow[qq] = out[qq];
+        }
+        // Release the slot only after this warp's reads of it have completed (the values
+        // are consumed by the stores above) and are ordered before the TMA (async proxy)
+        // that refills it; releasing right after issuing the loads let a slow warp read
+        // the next strip's data.
         fence_proxy_async();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.cdone[slot]);
-        if (leader) {
-          if (!wwait(&bars.cdone[slot], (gs / kUCSlots) & 1, abort, err, 49)) {
-            stop = true;
-            break;
-          }
-          tma_store_3d(&map_dst, cbox, cs, it.y0, it.mat);
-          tma_store_commit();
-          // The previous strip's store has finished reading its slot: hand the slot back.
-          asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-          if (gs > 0) mbar_arrive(&bars.cempty[(gs - 1) % kUCSlots]);
-        }
+        if (lane == 0) mbar_arrive(&bars.cempty[slot]);
       }
     }
-    if (leader) tma_store_wait_all();
   }
   tc_fence_before();
   __syncthreads();
@@ -912,11 +921,10 @@ cudaError_t run_wupdate(bool ident, const float* H, const float* src, float* dst
                         int n, int K, int bw, int c0, cudaStream_t s) {
   int* err = device_error_flag();
   if (err == nullptr) return cudaErrorInvalidValue;
-  CUtensorMap mv, msrc, mdst, mw0, mw1;
+  CUtensorMap msrc, mw0, mw1;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  if (!wmap(&mv, H, n, n, n, batch, 128, sw) || !wmap(&msrc, src, n, n, n, batch, 128, sw) ||
-      !wmap(&mdst, dst, n, n, n, batch, 128, sw) || !wmap(&mw0, w.w0, kWB, kWB, n, batch, 32, sw) ||
-      !wmap(&mw1, w.w1, kWB, kWB, n, batch, 32, sw))
+  if (!wmap(&msrc, src, n, n, n, batch, 128, sw) || !wmap(&mw0, w.w0, kWB, kWB, n, batch, kUTN, sw) ||
+      !wmap(&mw1, w.w1, kWB, kWB, n, batch, kUTN, sw))
     return cudaErrorInvalidValue;
   const int m = n - K;
   const int nstrips = (n - c0 + kUTN - 1) / kUTN;
@@ -933,10 +941,10 @@ cudaError_t run_wupdate(bool ident, const float* H, const float* src, float* dst
   LaunchTimer timer("wupdate_kernel", s, (double)batch * (8.0 * mm * nc + 4.0 * mm * kWB * ngroups),
                     (double)batch * 2.0 * mm * nc * kWB);
   if (ident)
-    wupdate_kernel<true><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, mdst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+    wupdate_kernel<true><<<grid, kUThreads, kSmemU, s>>>(H, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
                                                          ntiles, ngroups, gsize, err);
   else
-    wupdate_kernel<false><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, mdst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+    wupdate_kernel<false><<<grid, kUThreads, kSmemU, s>>>(H, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
                                                           ntiles, ngroups, gsize, err);
   return cudaGetLastError();
 }
@@ -946,11 +954,17 @@ cudaError_t run_wupdate(bool ident, const float* H, const float* src, float* dst
 bool wide_supported(int n) { return n % 4 == 0 && n >= kWideMinN && encode_fn_w() != nullptr; }
 
 size_t wide_ws_floats(int64_t batch, int n) {
+  // Y partials: the most row chunks any block's product uses, over both the full-width
+  // product (columns [K, n)) and the Gram-only one (the block's own 128 columns, which
+  // has fewer strips and so may split its rows into more chunks).
   size_t ymax = 0;
   for (int K = 0; K < n; K += kWB) {
-    const YPlan p = y_plan(batch, n, K, n);
-    const size_t y = (size_t)p.nsplit * batch * ycols(n) * kWB;
-    if (y > ymax) ymax = y;
+    const int bw = n - K < kWB ? n - K : kWB;
+    for (const int cend : {n, K + bw}) {
+      const YPlan p = y_plan(batch, n, K, cend);
+      const size_t y = (size_t)p.nsplit * batch * ycols(n) * kWB;
+      if (y > ymax) ymax = y;
+    }
   }
   const size_t mat = (size_t)batch * n * kWB;
   return al((size_t)nblocks(n) * batch * kWB * kWB) + 4 * al(mat) + al(ymax);

@@ -54,11 +54,13 @@ def _wide_floats(batch, n, sms=148):
     ymax = 0
     for K in range(0, n, 128):
         m = n - K
-        nstrips = (n - K + 127) // 128
-        ns = max(1, min(-(-2 * sms // (nstrips * batch)), (m + 511) // 512, 8))
-        chunk = (-(-m // ns) + 31) // 32 * 32
-        ns = -(-m // chunk)
-        ymax = max(ymax, ns * batch * nblk * 128 * 128)
+        bw = min(128, n - K)
+        for cend in (n, K + bw):        # full-width product and the Gram-only one
+            nstrips = (cend - K + 127) // 128
+            ns = max(1, min(-(-2 * sms // (nstrips * batch)), (m + 511) // 512, 8))
+            chunk = (-(-m // ns) + 31) // 32 * 32
+            ns = -(-m // chunk)
+            ymax = max(ymax, ns * batch * nblk * 128 * 128)
     return al(nblk * batch * 128 * 128) + 4 * al(batch * n * 128) + al(ymax)
 
 
