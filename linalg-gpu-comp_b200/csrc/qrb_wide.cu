@@ -22,12 +22,12 @@
 //                   Gram matrix: T_ab = -T_aa sum_{a<c<=b} G_ac T_cb.
 //   w2build_kernel  W2[c][a] = sum_j op(T)[a][j] Y[c][j] in fp32, stored as two tf32
 //                   pieces [batch][n][128] (the K-major B operand of the update).
-//   wupdate_kernel  C -= V W2: persistent CTAs over (matrix, 128-row tile, strip
-//                   group); the tile's V pieces live in tensor memory (the MMA's A
-//                   operand), C strips of 64 columns (three-slot ring) and their W2
-//                   pieces (two-slot ring) stream in by TMA, M=128 N=64 K=8 MMAs into
-//                   four TMEM accumulators; the epilogue subtracts and writes each
-//                   finished row to global memory directly.
+//   wupdate_kernel  C -= V W2: persistent CTA pairs over (matrix, 256-row tile, strip
+//                   group); each CTA's 128 rows of V live in its tensor memory (the
+//                   MMA's A operand), C strips of 64 columns (three-slot ring) and
+//                   half of their W2 pieces (two-slot ring) stream in by TMA, the
+//                   leader issues M=256 N=64 K=8 pair MMAs into four TMEM
+//                   accumulators; the epilogue subtracts and stores coalesced rows.
 //
 // Every wait on another role of the CTA is bounded (mbar_wait_abort): a wait that runs
 // out records an error code in g_qrb_device_error and raises a CTA-wide abort flag;
@@ -481,33 +481,40 @@ w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int n
   }
 }
 
-// ---- wupdate: C -= V W2 with V in tensor memory -------------------------------------------------
-// Warp roles: 0 = C producer, 1 = MMA issuer (TMEM owner), 2-5 = epilogue (they also
-// load each item's V tile, one row per thread, and split it into the tensor memory),
-// 6 = W2 producer.  C strips (the HBM stream) and W2 pieces (re-read from L2 by every
-// row tile) flow through separate rings, so C loads run several strips ahead of the
-// MMAs and W2 loads several strips ahead of their L2 latency; four TMEM accumulators
-// let the MMAs run ahead of the epilogue.
-// Strips are 64 columns: a tf32 MMA costs at least ~44 cycles whatever its N (measured
-// on B200: M=128 N=32 K=8 44.6 cycles, N=64 ~46, N=128 64, N=256 128), so N=32 strips
-// would cap the kernel near 4.4 TB/s on the MMA issue alone.
+// ---- wupdate: C -= V W2 with V in tensor memory, by CTA pairs -----------------------------
+// A 2-CTA cluster owns 256 rows (128 per CTA) of one matrix and a group of 64-column
+// strips.  Each CTA splits its 128 x 128 V tile into its own tensor memory; the even
+// (leader) CTA issues M=256 N=64 K=8 pair MMAs (cta_group::2) whose B operand -- the
+// strip's W2 pieces -- is split along N between the two CTAs' shared memory, so each
+// CTA streams only half of W2 per strip: as many W2 bytes from L2 as C bytes from HBM.
+// (With single-CTA M=128 tiles W2 traffic was twice the C traffic and its L2 latency
+// set the pace; a tf32 MMA also costs at least ~44 cycles whatever its N, so N=32
+// strips were MMA-issue-bound.)
+// Warp roles per CTA: 0 = C and V producer, 1 = MMA issuer (leader) and TMEM owner,
+// 2-5 and 7-10 = two epilogue warpgroups taking alternate strips (C -= V W2; the first
+// also splits each item's V tile into the tensor memory), 6 = W2 producer.
+// Barriers the MMA waits on live in the leader (W2 landed in both CTAs, both CTAs'
+// epilogues done with an accumulator, both V tiles ready); the leader's commits arrive
+// in both CTAs.
 constexpr int kUCSlots = 3;
 constexpr int kUWSlots = 2;
 constexpr int kUAcc = 4;
-constexpr int kUTN = 64;                           // strip width (N)
+constexpr int kUTN = 64;                           // strip width (N of the pair MMA)
+constexpr int kUHalf = kUTN / 2;                   // W2 columns each CTA holds
 constexpr uint32_t kUCBox = 128 * 128;             // 128 rows x 32 fp32
 constexpr uint32_t kUCSlot = 2 * kUCBox;           // one C strip: 128 rows x 64 columns
-constexpr uint32_t kUOffW = 0;
-constexpr uint32_t kUWBox = kUTN * 128;            // 64 columns x 32 K values
+constexpr uint32_t kUOffV = 0;                     // V staging: 4 boxes of 128 rows x 32
+constexpr uint32_t kUWBox = kUHalf * 128;          // 32 columns x 32 K values
 constexpr uint32_t kUWPiece = 4 * kUWBox;          // K = 128
-constexpr uint32_t kUWSlot = 2 * kUWPiece;         // two tf32 pieces
+constexpr uint32_t kUWSlot = 2 * kUWPiece;         // two tf32 pieces (16 KB each)
+constexpr uint32_t kUOffW = kUOffV + 4 * kUCBox;
 constexpr uint32_t kUOffC = kUOffW + kUWSlots * kUWSlot;
 constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUCSlot;
 constexpr uint32_t kSmemU = kUBarOff + 512 + 1024;
-constexpr int kUThreads = 224;
+constexpr int kUThreads = 352;
 
 struct UBars {
-  uint64_t cfull[kUCSlots], cempty[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vready,
+  uint64_t cfull[kUCSlots], cempty[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vfull, vempty, vready,
       accf[kUAcc], acce[kUAcc], drain;
   uint32_t tmem;
   int abort;
@@ -516,14 +523,14 @@ static_assert(sizeof(UBars) <= 512, "barrier block");
 static_assert(kSmemU <= 232448, "shared memory");
 
 struct UItem {
-  int mat, y0, s0, s1;
+  int mat, y0, s0, s1;   // y0: first row of the pair's 256-row tile
 };
 
 __device__ __forceinline__ UItem u_item(int64_t item, int K, int ntiles, int ngroups, int gsize, int nstrips) {
   UItem it;
   const int g = (int)(item % ngroups);
   const int64_t t = item / ngroups;
-  it.y0 = K + (int)(t % ntiles) * 128;
+  it.y0 = K + (int)(t % ntiles) * 256;
   it.mat = (int)(t / ntiles);
   it.s0 = g * gsize;
   it.s1 = min(nstrips, it.s0 + gsize);
@@ -531,19 +538,22 @@ __device__ __forceinline__ UItem u_item(int64_t item, int K, int ntiles, int ngr
 }
 
 template <bool IDENT>
-__global__ void __launch_bounds__(kUThreads, 1)
-wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap map_src, float* dst,
-               const __grid_constant__ CUtensorMap map_w0,
-               const __grid_constant__ CUtensorMap map_w1, int64_t batch, int n, int K, int bw, int c0, int nstrips,
-               int ntiles, int ngroups, int gsize, int* err) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kUThreads, 1)
+wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_src, float* dst,
+               const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1, int64_t batch,
+               int n, int K, int bw, int c0, int nstrips, int ntiles, int ngroups, int gsize, int* err) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                        ~uintptr_t(1023));
   UBars& bars = *reinterpret_cast<UBars*>(sm + kUBarOff);
   volatile int* abort = &bars.abort;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   const int kb = K + bw;
   const int64_t nitems = batch * ntiles * ngroups;
+  const int64_t pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int rowoff = 128 * (int)rank;   // this CTA's rows within the pair's tile
 
   if (tid == 0) {
     for (int i = 0; i < kUCSlots; ++i) {
@@ -554,33 +564,47 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
       mbar_init(&bars.wfull[i], 1);
       mbar_init(&bars.wempty[i], 1);
     }
-    mbar_init(&bars.vready, 4);
+    mbar_init(&bars.vfull, 1);
+    mbar_init(&bars.vempty, 4);
+    mbar_init(&bars.vready, 8);   // both CTAs' epilogue warps (leader's copy is used)
     for (int i = 0; i < kUAcc; ++i) {
       mbar_init(&bars.accf[i], 1);
-      mbar_init(&bars.acce[i], 4);
+      mbar_init(&bars.acce[i], 8);   // both CTAs' epilogue warps (leader's copy is used)
     }
     mbar_init(&bars.drain, 1);
     bars.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(&bars.tmem, 512);
+  if (warp == 1) tmem_alloc_pair(&bars.tmem, 512);
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();   // the peer's barriers exist before anything is signalled across the pair
   tc_fence_after();
   const uint32_t tmem = bars.tmem;
   constexpr uint32_t kAcc = 256;   // accumulators after the two V pieces (128 columns each)
+  // The leader's copies of the barriers both CTAs signal.
+  const uint32_t lead_wfull0 = mapa_shared(smem_u32(&bars.wfull[0]), 0);
+  const uint32_t lead_acce0 = mapa_shared(smem_u32(&bars.acce[0]), 0);
+  const uint32_t lead_vready = mapa_shared(smem_u32(&bars.vready), 0);
 
   if (warp == 0) {
-    // ---------------- C producer ----------------
+    // ---------------- C and V producer (each CTA, its own rows) ----------------
     if (lane == 0) {
       prefetch_tensormap(&map_src);
-      int gs = 0;
+      prefetch_tensormap(&map_v);
+      int gs = 0, iter = 0, v_last = -1;
       int last_use[kUCSlots];
 #pragma unroll
       for (int i = 0; i < kUCSlots; ++i) last_use[i] = -1;
       bool stop = false;
-      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+      for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+        const int y = it.y0 + rowoff;
+        if (iter > 0 && !wwait(&bars.vempty, (iter - 1) & 1, abort, err, 41)) break;
+        mbar_arrive_expect_tx(&bars.vfull, 4 * kUCBox);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tma_load_3d(sm + kUOffV + j * kUCBox, &map_v, K + 32 * j, y, it.mat, &bars.vfull);
+        v_last = iter;
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kUCSlots, use = gs / kUCSlots;
           if (use > 0 && !wwait(&bars.cempty[slot], (use - 1) & 1, abort, err, 42)) {
@@ -589,18 +613,19 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
           }
           mbar_arrive_expect_tx(&bars.cfull[slot], kUCSlot);
           unsigned char* cb = sm + kUOffC + slot * kUCSlot;
-          tma_load_3d(cb, &map_src, c0 + s * kUTN, it.y0, it.mat, &bars.cfull[slot]);
-          tma_load_3d(cb + kUCBox, &map_src, c0 + s * kUTN + 32, it.y0, it.mat, &bars.cfull[slot]);
+          tma_load_3d(cb, &map_src, c0 + s * kUTN, y, it.mat, &bars.cfull[slot]);
+          tma_load_3d(cb + kUCBox, &map_src, c0 + s * kUTN + 32, y, it.mat, &bars.cfull[slot]);
           last_use[slot] = use;
         }
       }
       if (*abort) {   // let every load this CTA issued land before its shared memory goes away
+        if (v_last >= 0) mbar_wait(&bars.vfull, v_last & 1, 1u << 22);
         for (int sl = 0; sl < kUCSlots; ++sl)
           if (last_use[sl] >= 0) mbar_wait(&bars.cfull[sl], last_use[sl] & 1, 1u << 22);
       }
     }
   } else if (warp == 6) {
-    // ---------------- W2 producer ----------------
+    // ---------------- W2 producer (each CTA, its half of the strip's columns) ----------------
     if (lane == 0) {
       prefetch_tensormap(&map_w0);
       prefetch_tensormap(&map_w1);
@@ -609,7 +634,7 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
 #pragma unroll
       for (int i = 0; i < kUWSlots; ++i) last_use[i] = -1;
       bool stop = false;
-      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x) {
+      for (int64_t item = pair; item < nitems && !stop; item += npairs) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kUWSlots, use = gs / kUWSlots;
@@ -618,32 +643,35 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
             break;
           }
           unsigned char* sl = sm + kUOffW + slot * kUWSlot;
-          const int cs = c0 + s * kUTN;
-          mbar_arrive_expect_tx(&bars.wfull[slot], kUWSlot);
+          const int cs = c0 + s * kUTN + kUHalf * (int)rank;
+          const uint32_t bar = lead_wfull0 + slot * (uint32_t)sizeof(uint64_t);
+          // The leader expects both halves' bytes; the peer's copies count on the leader's barrier.
+          if (leader) mbar_arrive_expect_tx(&bars.wfull[slot], 2 * kUWSlot);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            tma_load_3d(sl + j * kUWBox, &map_w0, 32 * j, cs, it.mat, &bars.wfull[slot]);
-            tma_load_3d(sl + kUWPiece + j * kUWBox, &map_w1, 32 * j, cs, it.mat, &bars.wfull[slot]);
+            tma_load_3d_pair(sl + j * kUWBox, &map_w0, 32 * j, cs, it.mat, bar);
+            tma_load_3d_pair(sl + kUWPiece + j * kUWBox, &map_w1, 32 * j, cs, it.mat, bar);
           }
           last_use[slot] = use;
         }
       }
-      if (*abort) {
-        for (int sl = 0; sl < kUWSlots; ++sl)
-          if (last_use[sl] >= 0) mbar_wait(&bars.wfull[sl], last_use[sl] & 1, 1u << 22);
-      }
+      (void)last_use;   // after an abort the leader's drain waits for both halves (see the MMA role)
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, kUTN, 0, 0);
+    // ---------------- MMA issuer (leader only) ----------------
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_tf32(256, kUTN, 0, 0);
       int gs = 0, iter = 0;
       bool issued = false, stop = false;
-      for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+      int w_last[kUWSlots];
+#pragma unroll
+      for (int i = 0; i < kUWSlots; ++i) w_last[i] = -1;
+      for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
         if (!wwait(&bars.vready, iter & 1, abort, err, 43)) break;
         for (int s = it.s0; s < it.s1; ++s, ++gs) {
           const int slot = gs % kUWSlots, acc = gs % kUAcc;
+          w_last[slot] = gs / kUWSlots;
           if (!wwait(&bars.wfull[slot], (gs / kUWSlots) & 1, abort, err, 44) ||
               (gs >= kUAcc && !wwait(&bars.acce[acc], ((gs / kUAcc) - 1) & 1, abort, err, 45))) {
             stop = true;
@@ -657,46 +685,51 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
 #pragma unroll
             for (int kk = 0; kk < 16; ++kk) {
               const uint32_t a = tmem + kWTermA[tt] * 128 + kk * 8;
+              // Each CTA's half: 32 rows (strip columns) x 32 K values per box, K-major.
               const uint64_t bd =
-                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);   // N = 64 rows
-              mma_tf32_ta(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
+                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);
+              mma_tf32_ta_pair(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          mma_commit(&bars.accf[acc]);
-          mma_commit(&bars.wempty[slot]);
+          mma_commit_pair(&bars.accf[acc]);
+          mma_commit_pair(&bars.wempty[slot]);
           issued = true;
         }
       }
-      if (*abort && issued) {   // tensor memory must not be released under running MMAs
-        mma_commit(&bars.drain);
-        mbar_wait(&bars.drain, 0, 1u << 22);
+      if (*abort) {
+        if (issued) {   // tensor memory must not be released under running MMAs
+          mma_commit_pair(&bars.drain);
+          mbar_wait(&bars.drain, 0, 1u << 22);
+        }
+        for (int sl = 0; sl < kUWSlots; ++sl)   // both CTAs' W2 copies have landed
+          if (w_last[sl] >= 0) mbar_wait(&bars.wfull[sl], w_last[sl] & 1, 1u << 22);
       }
     }
   } else {
-    // ---------------- epilogue warps 2-5: V into tensor memory, then C -= V W2 ----------------
+    // ---------------- epilogue warpgroups (warps 2-5: wg 0, 7-10: wg 1) ----------------
+    const int wg = warp >= 7 ? 1 : 0;
     const int q = warp & 3;
-    const int r = 32 * q + lane;   // tile row = TMEM lane
+    const int r = 32 * q + lane;   // row within this CTA's 128 = TMEM lane
     const uint32_t tl = (uint32_t)(32 * q) << 16;
     int gs = 0, iter = 0;
     bool stop = false;
-    for (int64_t item = blockIdx.x; item < nitems && !stop; item += gridDim.x, ++iter) {
+    for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
       const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
-      const int R = it.y0 + r;
-      if (*abort) break;
-      // V row R of the block (row R - K of the reflectors), masked to the unit lower
-      // trapezoid; rows past n are zero.  The MMAs of the previous item have completed
-      // (its last accumulator was read), so the tensor memory may be overwritten.
-      const float4* vrow = reinterpret_cast<const float4*>(H + ((size_t)it.mat * n + R) * n + K);
+      const int y = it.y0 + rowoff;
+      const int R = y + r;
+      if (wg == 0) {
+      // V rows of this CTA, masked to the unit lower trapezoid, split into the tensor
+      // memory once the previous item's MMAs have completed (the accumulator of its
+      // last strip, whichever warpgroup reads it, has been written).
+      if (gs > 0 && !wwait(&bars.accf[(gs - 1) % kUAcc], ((gs - 1) / kUAcc) & 1, abort, err, 51)) break;
+      if (!wwait(&bars.vfull, iter & 1, abort, err, 46)) break;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float x0[32], x1[32];
-        float4 vv[8];
-#pragma unroll
-        for (int qq = 0; qq < 8; ++qq)
-          vv[qq] = (R < n && 32 * c + 4 * qq < bw) ? __ldg(vrow + 8 * c + qq) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const unsigned char* box = sm + kUOffV + c * kUCBox;
 #pragma unroll
         for (int qq = 0; qq < 8; ++qq) {
-          const float4 v = vv[qq];
+          const float4 v = *reinterpret_cast<const float4*>(box + off128_w(r, qq));
           const float a[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e)
@@ -708,8 +741,13 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bars.vready);
+      if (lane == 0) {
+        mbar_arrive(&bars.vempty);               // staging free for the next item's V
+        mbar_arrive_cluster(lead_vready);        // this CTA's quarter of V is in TMEM
+      }
+      }
       for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        if ((gs & 1) != wg) continue;
         const int slot = gs % kUCSlots, acc = gs % kUAcc;
         const int cs = c0 + s * kUTN;
         unsigned char* cbox = sm + kUOffC + slot * kUCSlot;
@@ -724,15 +762,16 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
         tmem_ld32(tmem + tl + kAcc + acc * kUTN + 32, d[1]);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.acce[acc]);
-        // Row R of the strip: C - V W2, written straight to global memory (one 256-byte
-        // row per thread); no shared-memory write-back or bulk store is needed.
-        float4 out[16];
+        if (lane == 0) mbar_arrive_cluster(lead_acce0 + acc * (uint32_t)sizeof(uint64_t));
+        // Row R of the strip: C - V W2 is written back in place into the slot, then the
+        // warp stores its 32 rows to global memory coalesced (lanes 0-15 and 16-31 each
+        // cover one 256-byte row per instruction).
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
           for (int qq = 0; qq < 8; ++qq) {
-            const float4 cv4 = *reinterpret_cast<const float4*>(cbox + h * kUCBox + off128_w(r, qq));
+            float4* cp = reinterpret_cast<float4*>(cbox + h * kUCBox + off128_w(r, qq));
+            const float4 cv4 = *cp;
             float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -742,16 +781,23 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
               }
               cv[e] -= d[h][4 * qq + e];
             }
-            out[8 * h + qq] = make_float4(cv[0], cv[1], cv[2], cv[3]);
+            *cp = make_float4(cv[0], cv[1], cv[2], cv[3]);
           }
         }
-        if (R < n) {
-          float4* drow = reinterpret_cast<float4*>(dst + ((size_t)it.mat * n + R) * n + cs);
-#pragma unroll
-          for (int qq = 0; qq < 16; ++qq)
-            if (cs + 4 * qq < n) drow[qq] = out[qq];
+        __syncwarp();
+        {
+          const int sub = lane >> 4, q4 = lane & 15;   // row parity, float4 column 0..15
+          const int h = q4 >> 3, qq = q4 & 7;
+#pragma unroll 4
+          for (int i = 0; i < 16; ++i) {
+            const int rr = 32 * q + 2 * i + sub;       // tile row written by this lane
+            const int Rg = y + rr;
+            const float4 v = *reinterpret_cast<const float4*>(cbox + h * kUCBox + off128_w(rr, qq));
+            if (Rg < n && cs + 4 * q4 < n)
+              *reinterpret_cast<float4*>(dst + ((size_t)it.mat * n + Rg) * n + cs + 4 * q4) = v;
+          }
         }
-        // Release the slot only after this warp's reads of it have completed (the values
+        // Release the slot only after this warp's reads of it have completed (their values
         // are consumed by the stores above) and are ordered before the TMA (async proxy)
         // that refills it; releasing right after issuing the loads let a slow warp read
         // the next strip's data.
@@ -763,9 +809,10 @@ wupdate_kernel(const float* __restrict__ H, const __grid_constant__ CUtensorMap 
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();   // neither CTA leaves while the pair's MMAs or signals may touch it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -921,30 +968,32 @@ cudaError_t run_wupdate(bool ident, const float* H, const float* src, float* dst
                         int n, int K, int bw, int c0, cudaStream_t s) {
   int* err = device_error_flag();
   if (err == nullptr) return cudaErrorInvalidValue;
-  CUtensorMap msrc, mw0, mw1;
+  CUtensorMap mv, msrc, mw0, mw1;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  if (!wmap(&msrc, src, n, n, n, batch, 128, sw) || !wmap(&mw0, w.w0, kWB, kWB, n, batch, kUTN, sw) ||
-      !wmap(&mw1, w.w1, kWB, kWB, n, batch, kUTN, sw))
+  if (!wmap(&mv, H, n, n, n, batch, 128, sw) || !wmap(&msrc, src, n, n, n, batch, 128, sw) ||
+      !wmap(&mw0, w.w0, kWB, kWB, n, batch, kUHalf, sw) || !wmap(&mw1, w.w1, kWB, kWB, n, batch, kUHalf, sw))
     return cudaErrorInvalidValue;
   const int m = n - K;
   const int nstrips = (n - c0 + kUTN - 1) / kUTN;
-  const int ntiles = (m + 127) / 128;
+  const int ntiles = (m + 255) / 256;   // 256-row tiles, one per CTA pair
   const int64_t tiles = batch * ntiles;
-  const int sms = sm_count();
-  int ngroups = (int)((4 * (int64_t)sms + tiles - 1) / tiles);
+  const int pairs = sm_count() / 2;
+  // At least four items per pair so the last round is short; strip groups (each
+  // reloading V) only when there are too few row tiles for that.
+  int ngroups = (int)((4 * (int64_t)pairs + tiles - 1) / tiles);
   ngroups = ngroups < 1 ? 1 : (ngroups > nstrips ? nstrips : ngroups);
   const int gsize = (nstrips + ngroups - 1) / ngroups;
   ngroups = (nstrips + gsize - 1) / gsize;
   const int64_t items = tiles * ngroups;
-  const unsigned grid = (unsigned)(items < sms ? items : sms);
+  const unsigned grid = 2u * (unsigned)(items < pairs ? items : pairs);
   const double mm = m, nc = n - c0;
   LaunchTimer timer("wupdate_kernel", s, (double)batch * (8.0 * mm * nc + 4.0 * mm * kWB * ngroups),
                     (double)batch * 2.0 * mm * nc * kWB);
   if (ident)
-    wupdate_kernel<true><<<grid, kUThreads, kSmemU, s>>>(H, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+    wupdate_kernel<true><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
                                                          ntiles, ngroups, gsize, err);
   else
-    wupdate_kernel<false><<<grid, kUThreads, kSmemU, s>>>(H, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
+    wupdate_kernel<false><<<grid, kUThreads, kSmemU, s>>>(mv, msrc, dst, mw0, mw1, batch, n, K, bw, c0, nstrips,
                                                           ntiles, ngroups, gsize, err);
   return cudaGetLastError();
 }
