@@ -285,7 +285,7 @@ def roofline_from_profile(prof: dict, steps: int, step_ms: float, n: int, batch:
     gbs = d["bytes"] / (d["ms"] / 1e3) / 1e9
     tf32_peak = peaks["bf16_tflops_sustained"] / 2.0
     # 3xTF32: the tensor-core kernels issue three tf32 products per useful multiply-add.
-    tensor_kernel = name in ("wpart_kernel", "update_kernel", "ygemm_kernel", "wupdate_kernel")
+    tensor_kernel = name in ("wpart_kernel", "update_kernel", "ygemm_kernel", "wupdate_kernel", "w2tc_kernel")
     k_tflops = (3.0 if tensor_kernel else 1.0) * d["flops"] / (d["ms"] / 1e3) / 1e12
     step_tflops = batch * flops_per_matrix(n) / (step_ms / 1e3) / 1e12
     return {

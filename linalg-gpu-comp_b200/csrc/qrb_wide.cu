@@ -20,8 +20,9 @@
 //                   matrix V^T V of the block.
 //   tbuild_kernel   T (128 x 128) of the block from the four panel T factors and the
 //                   Gram matrix: T_ab = -T_aa sum_{a<c<=b} G_ac T_cb.
-//   w2build_kernel  W2[c][a] = sum_j op(T)[a][j] Y[c][j] in fp32, stored as two tf32
-//                   pieces [batch][n][128] (the K-major B operand of the update).
+//   w2tc_kernel     W2[c][a] = sum_j op(T)[a][j] Y[c][j] on the tensor cores, stored
+//                   as two tf32 pieces [batch][n][128] (the K-major B operand of the
+//                   update).
 //   wupdate_kernel  C -= V W2: persistent CTA pairs over (matrix, 256-row tile, strip
 //                   group); each CTA's 128 rows of V live in its tensor memory (the
 //                   MMA's A operand), C strips of 64 columns (three-slot ring) and
@@ -384,100 +385,214 @@ tbuild_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int nc
   }
 }
 
-// ---- w2build: W2 = Y op(T)^T as two tf32 pieces ---------------------------------------------
-constexpr int kW2Cols = 64;
-constexpr uint32_t kSmemW2 = (128 * 132 + 128 * (kW2Cols + 4)) * 4;
+// ---- w2tc: W2 = Y op(T)^T on the tensor cores ------------------------------------------------
+// One CTA per (matrix, 128 columns): D[c][a] = sum_j Y[c][j] op(T)[a][j] as M=128 N=128
+// K=8 tf32 MMAs (3xTF32).  Y (the columns' rows of the Y partials, summed over the row
+// chunks) is split into the tensor memory (A operand, lane = column); op(T)^T is staged
+// by TMA and split in place in shared memory (B operand: T itself for geqrf, which is
+// then MN-major, or T^T for orgqr, K-major); the result is split into the two W2 pieces
+// and leaves through TMA stores.  Replaces w2build_kernel's fp32 SIMT product.
+constexpr uint32_t kW2TBox32 = 32 * 128;      // 32 rows x 32 fp32
+constexpr uint32_t kW2TBox128 = 128 * 128;    // 128 rows x 32 fp32
+constexpr uint32_t kW2TPiece = 4 * kW2TBox128;   // 64 KB: a 128 x 128 operand
+constexpr uint32_t kW2TOffY = 2 * kW2TPiece;     // T pieces first, then the raw Y tile
+constexpr uint32_t kW2TBar = kW2TOffY + kW2TPiece;
+constexpr uint32_t kSmemW2T = kW2TBar + 64 + 1024;
 
-__global__ void __launch_bounds__(256)
-w2build_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int ncolsY, int n, int K, int cfirst,
-               int ngroups, const float* __restrict__ t128, float* __restrict__ w2p0, float* __restrict__ w2p1,
-               int trans_t) {
-  extern __shared__ float smw[];
-  float(*Ot)[132] = reinterpret_cast<float(*)[132]>(smw);                     // Ot[j][a] = op(T)[a][j]
-  float(*Yt)[kW2Cols + 4] = reinterpret_cast<float(*)[kW2Cols + 4]>(smw + 128 * 132);   // Yt[j][i]
-  const int tid = threadIdx.x;
-  const int64_t mat = blockIdx.x / ngroups;
-  const int c0 = cfirst + (int)(blockIdx.x % ngroups) * kW2Cols;
-  // T (16 float4 per thread) and the Y strip (8 float4 per thread, summed over the row
-  // chunks), every load of a batch in flight before the shared-memory stores.
-  {
-    const float4* T4 = reinterpret_cast<const float4*>(t128 + (size_t)mat * kWB * kWB);
-    float4 t[16];
-#pragma unroll
-    for (int k = 0; k < 16; ++k) t[k] = __ldg(T4 + tid + 256 * k);
-#pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int u = tid + 256 * k, r = u >> 5, c = 4 * (u & 31);
-      const float v[4] = {t[k].x, t[k].y, t[k].z, t[k].w};
-      if (trans_t) {   // op(T) = T^T: Ot[j][a] = T[j][a]
-        *reinterpret_cast<float4*>(&Ot[r][c]) = t[k];
-      } else {         // op(T) = T:   Ot[j][a] = T[a][j]
-#pragma unroll
-        for (int e = 0; e < 4; ++e) Ot[c + e][r] = v[e];
-      }
+template <int TRANS>
+__global__ void __launch_bounds__(128, 1)
+w2tc_kernel(const __grid_constant__ CUtensorMap map_t, const __grid_constant__ CUtensorMap map_y,
+            const __grid_constant__ CUtensorMap map_w0, const __grid_constant__ CUtensorMap map_w1, int64_t batch,
+            int n, int K, int cfirst, int ngroups, int nsplit, int blk, int* err) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                       ~uintptr_t(1023));
+  uint64_t* tbar = reinterpret_cast<uint64_t*>(sm + kW2TBar);
+  uint64_t* ybar = tbar + 1;
+  uint64_t* mbar = tbar + 2;   // two: one per accumulator buffer
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(tbar + 4);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int mat = (int)(blockIdx.x / ngroups);
+  const int cg = cfirst + (int)(blockIdx.x % ngroups) * 128;   // first column of the group
+  const int zt = blk * (int)batch + mat;                        // T factor index (block, matrix)
+
+  if (tid == 0) {
+    mbar_init(tbar, 1);
+    mbar_init(ybar, 1);
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
+    fence_mbar_init();
+    prefetch_tensormap(&map_t);
+    prefetch_tensormap(&map_y);
+    // T lands raw in piece 0; geqrf: 16 boxes (32 a x 32 j rows, MN-major B, 32-byte
+    // atoms), orgqr: 4 boxes (32 j x 128 a rows, K-major B).
+    mbar_arrive_expect_tx(tbar, kW2TPiece);
+    if (TRANS) {
+      for (int jb = 0; jb < 4; ++jb)
+        for (int ab = 0; ab < 4; ++ab)
+          tma_load_3d(sm + (jb * 4 + ab) * kW2TBox32, &map_t, 32 * ab, 32 * jb, zt, tbar);
+    } else {
+      for (int jb = 0; jb < 4; ++jb) tma_load_3d(sm + jb * kW2TBox128, &map_t, 32 * jb, 0, zt, tbar);
     }
-    // Lane = column here (consecutive lanes store consecutive columns of a Yt row, so
-    // the transposing shared-memory stores do not conflict).
-    float4 y[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) y[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float* base = ypart + ((size_t)sp * batch + mat) * ncolsY * kWB;
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int u = tid + 256 * k, i = u & 63, j = 4 * (u >> 6);
-        if (c0 + i < n) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(base + (size_t)(c0 + i - K) * kWB + j));
-          y[k].x += v.x;
-          y[k].y += v.y;
-          y[k].z += v.z;
-          y[k].w += v.w;
-        }
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int u = tid + 256 * k, i = u & 63, j = 4 * (u >> 6);
-      Yt[j][i] = y[k].x;
-      Yt[j + 1][i] = y[k].y;
-      Yt[j + 2][i] = y[k].z;
-      Yt[j + 3][i] = y[k].w;
-    }
+    mbar_arrive_expect_tx(ybar, kW2TPiece);
+    for (int jb = 0; jb < 4; ++jb)
+      tma_load_3d(sm + kW2TOffY + jb * kW2TBox128, &map_y, 32 * jb, cg - K, mat, ybar);
   }
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
   __syncthreads();
-  const int i0 = 4 * (tid & 15), a0 = 8 * (tid >> 4);
-  // op(T) is lower triangular for geqrf (T^T: j <= a) and upper for orgqr (j >= a).
-  const int jlo = trans_t ? 0 : a0, jhi = trans_t ? a0 + 8 : 128;
-  float acc[4][8];
-#pragma unroll
-  for (int x = 0; x < 4; ++x)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[x][e] = 0.f;
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = (uint32_t)(32 * warp) << 16;
+  bool bad = false;
+
+  // ---- T -> two tf32 pieces in place (piece 1 64 KB further) ----
+  bad = !mbar_wait(tbar, 0);
+  if (!__syncthreads_or(bad)) {
 #pragma unroll 4
-  for (int j = jlo; j < jhi; ++j) {
-    const float4 yv = *reinterpret_cast<const float4*>(&Yt[j][i0]);
-    const float4 oa = *reinterpret_cast<const float4*>(&Ot[j][a0]);
-    const float4 ob = *reinterpret_cast<const float4*>(&Ot[j][a0 + 4]);
-    const float yy[4] = {yv.x, yv.y, yv.z, yv.w};
-    const float oo[8] = {oa.x, oa.y, oa.z, oa.w, ob.x, ob.y, ob.z, ob.w};
+    for (int i = 0; i < 32; ++i) {
+      const int u = tid + 128 * i;   // float4 index 0..4095
+      uint32_t off;
+      if (TRANS) {
+        const int bx = u >> 8, r = (u >> 3) & 31, q = u & 7;
+        off = bx * kW2TBox32 + off32b_w(r, q);
+      } else {
+        const int bx = u >> 10, r = (u >> 3) & 127, q = u & 7;
+        off = bx * kW2TBox128 + off128_w(r, q);
+      }
+      const float4 v = *reinterpret_cast<const float4*>(sm + off);
+      const float a4[4] = {v.x, v.y, v.z, v.w};
+      float x0[4], x1[4];
 #pragma unroll
-    for (int x = 0; x < 4; ++x)
+      for (int e = 0; e < 4; ++e) split2_tf32(a4[e], x0[e], x1[e]);
+      *reinterpret_cast<float4*>(sm + off) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+      *reinterpret_cast<float4*>(sm + kW2TPiece + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+    }
+    fence_proxy_async();
+  } else {
+    bad = true;
+  }
+
+  // ---- Y rows (thread = column), summed over the row chunks, into the tensor memory ----
+  float y[128];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[x][e] = fmaf(oo[e], yy[x], acc[x][e]);
+  for (int j = 0; j < 128; ++j) y[j] = 0.f;
+  for (int sp = 0; sp < nsplit && !bad; ++sp) {
+    bad = !mbar_wait(ybar, sp & 1);
+    if (__syncthreads_or(bad)) {
+      bad = true;
+      break;
+    }
+#pragma unroll
+    for (int jb = 0; jb < 4; ++jb)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 v = *reinterpret_cast<const float4*>(sm + kW2TOffY + jb * kW2TBox128 + off128_w(tid, q));
+        y[32 * jb + 4 * q] += v.x;
+        y[32 * jb + 4 * q + 1] += v.y;
+        y[32 * jb + 4 * q + 2] += v.z;
+        y[32 * jb + 4 * q + 3] += v.w;
+      }
+    __syncthreads();   // every row read before the next partial overwrites the tile
+    if (tid == 0 && sp + 1 < nsplit) {
+      mbar_arrive_expect_tx(ybar, kW2TPiece);
+      for (int jb = 0; jb < 4; ++jb)
+        tma_load_3d(sm + kW2TOffY + jb * kW2TBox128, &map_y, 32 * jb, cg - K, (sp + 1) * (int)batch + mat, ybar);
+    }
+  }
+  if (!bad) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float x0[32], x1[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) split2_tf32(y[32 * c + j], x0[j], x1[j]);
+      tmem_st32(tmem + tl + 32 * c, x0);
+      tmem_st32(tmem + tl + 128 + 32 * c, x1);
+    }
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  bad = __syncthreads_or(bad);
+  // Four K stages of 32 (12 MMAs each, small products first) into two alternating TMEM
+  // accumulators; the stage partials are summed in fp32 registers (reusing y[]).  One
+  // long tensor-core accumulation rounds every add against the running sum and costs
+  // accuracy (orthogonality at n = 2048 5.7e-6 against 3.7e-6 with stages).
+  constexpr uint32_t idesc = idesc_tf32(128, 128, 0, TRANS ? 1 : 0);
+  auto issue_stage = [&](int st) {
+    tc_fence_after();
+    const uint32_t tb = smem_u32(sm);
+    const uint32_t d = tmem + 256 + (st & 1) * 128;
+#pragma unroll
+    for (int tt = 0; tt < 3; ++tt) {
+#pragma unroll
+      for (int k4 = 0; k4 < 4; ++k4) {
+        const int kk = 4 * st + k4;
+        const uint32_t bb = tb + kWTermB[tt] * kW2TPiece;
+        const uint64_t bd = TRANS ? sdesc_sw128_32b(bb + (kk >> 2) * 4 * kW2TBox32 + (kk & 3) * 1024, kW2TBox32, 512)
+                                  : sdesc_sw128(bb + (kk >> 2) * kW2TBox128 + (kk & 3) * 32, 16, 1024);
+        mma_tf32_ta(d, tmem + kWTermA[tt] * 128 + kk * 8, bd, idesc, (tt > 0 || k4 > 0) ? 1u : 0u);
+      }
+    }
+    mma_commit(&mbar[st & 1]);
+  };
+  if (!bad && tid == 0) {
+    issue_stage(0);
+    issue_stage(1);
   }
 #pragma unroll
-  for (int x = 0; x < 4; ++x) {
-    const int c = c0 + i0 + x;
-    if (c >= n) continue;
-    float p0[8], p1[8];
+  for (int j = 0; j < 128; ++j) y[j] = 0.f;
+  for (int st = 0; st < 4 && !bad; ++st) {
+    bad = !mbar_wait(&mbar[st & 1], (st >> 1) & 1);
+    if (__syncthreads_or(bad)) {
+      bad = true;
+      if (tid == 0) atomicCAS(err, 0, 61);
+      break;
+    }
+    tc_fence_after();
 #pragma unroll
-    for (int e = 0; e < 8; ++e) split2_tf32(acc[x][e], p0[e], p1[e]);
-    float4* d0 = reinterpret_cast<float4*>(w2p0 + ((size_t)mat * n + c) * kWB + a0);
-    float4* d1 = reinterpret_cast<float4*>(w2p1 + ((size_t)mat * n + c) * kWB + a0);
-    d0[0] = make_float4(p0[0], p0[1], p0[2], p0[3]);
-    d0[1] = make_float4(p0[4], p0[5], p0[6], p0[7]);
-    d1[0] = make_float4(p1[0], p1[1], p1[2], p1[3]);
-    d1[1] = make_float4(p1[4], p1[5], p1[6], p1[7]);
+    for (int c = 0; c < 4; ++c) {
+      float d[32];
+      tmem_ld32(tmem + tl + 256 + (st & 1) * 128 + 32 * c, d);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) y[32 * c + j] += d[j];
+    }
+    tc_fence_before();
+    __syncthreads();   // the buffer is read by every warp before stage st + 2 overwrites it
+    if (tid == 0 && st + 2 < 4) issue_stage(st + 2);
+  }
+  bad = __syncthreads_or(bad);
+  if (!bad) {
+    // W2 row c (this thread's column) -> pieces, staged K-major over the T buffers (free:
+    // every MMA has completed) for the stores.
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float x0[4], x1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) split2_tf32(y[32 * c + 4 * q + e], x0[e], x1[e]);
+        const uint32_t off = c * kW2TBox128 + off128_w(tid, q);
+        *reinterpret_cast<float4*>(sm + off) = make_float4(x0[0], x0[1], x0[2], x0[3]);
+        *reinterpret_cast<float4*>(sm + kW2TPiece + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+      }
+    }
+    fence_proxy_async();
+  }
+  tc_fence_before();
+  bad = __syncthreads_or(bad);
+  if (!bad && tid == 0) {
+    for (int c = 0; c < 4; ++c) {
+      tma_store_3d(&map_w0, sm + c * kW2TBox128, 32 * c, cg, mat);
+      tma_store_3d(&map_w1, sm + kW2TPiece + c * kW2TBox128, 32 * c, cg, mat);
+    }
+    tma_store_commit();
+    tma_store_wait_all();
+  }
+  if (bad && tid == 0) atomicCAS(err, 0, 60);
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -903,7 +1018,8 @@ bool set_smem_attrs() {
       cudaFuncSetAttribute(wupdate_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemU) !=
           cudaSuccess ||
       cudaFuncSetAttribute(tbuild_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemT) != cudaSuccess ||
-      cudaFuncSetAttribute(w2build_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemW2) != cudaSuccess)
+      cudaFuncSetAttribute(w2tc_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemW2T) != cudaSuccess ||
+      cudaFuncSetAttribute(w2tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemW2T) != cudaSuccess)
     return false;
   done.fetch_or(bit, std::memory_order_acq_rel);
   return true;
@@ -953,14 +1069,30 @@ cudaError_t run_tbuild(const WideWs& w, const YPlan& plan, const float* t32blk, 
 
 cudaError_t run_w2build(const WideWs& w, const YPlan& plan, int blk, int64_t batch, int n, int K, int cfirst,
                         int trans_t, cudaStream_t s) {
-  const int ngroups = (n - cfirst + kW2Cols - 1) / kW2Cols;
+  const int ngroups = (n - cfirst + 127) / 128;
   if (ngroups <= 0) return cudaSuccess;
+  int* err = device_error_flag();
+  if (err == nullptr) return cudaErrorInvalidValue;
+  CUtensorMap mt, my, mw0, mw1;
+  const int nblk = nblocks(n);
+  // T factors [block][batch][128][128]: rows of 128 a (geqrf boxes 32 x 32 with 32-byte
+  // atoms; orgqr boxes 32 x 128); Y partials [split][batch][ncolsY][128]; W2 pieces.
+  const bool ok_t = trans_t ? wmap(&mt, w.t128, kWB, kWB, kWB, (uint64_t)nblk * batch, 32,
+                                   CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+                            : wmap(&mt, w.t128, kWB, kWB, kWB, (uint64_t)nblk * batch, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok_t || !wmap(&my, w.ypart, kWB, kWB, ycols(n), (uint64_t)plan.nsplit * batch, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !wmap(&mw0, w.w0, kWB, kWB, n, batch, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !wmap(&mw1, w.w1, kWB, kWB, n, batch, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
   const double nc = n - cfirst;
-  LaunchTimer timer("w2build_kernel", s, (double)batch * nc * kWB * 4.0 * (plan.nsplit + 2),
+  LaunchTimer timer("w2tc_kernel", s, (double)batch * nc * kWB * 4.0 * (plan.nsplit + 2) + batch * ngroups * 65536.0,
                     (double)batch * nc * kWB * kWB);
-  w2build_kernel<<<(unsigned)(batch * ngroups), 256, kSmemW2, s>>>(
-      w.ypart, plan.nsplit, batch, ycols(n), n, K, cfirst, ngroups, w.t128 + (size_t)blk * batch * kWB * kWB, w.w0,
-      w.w1, trans_t);
+  if (trans_t)
+    w2tc_kernel<1><<<(unsigned)(batch * ngroups), 128, kSmemW2T, s>>>(mt, my, mw0, mw1, batch, n, K, cfirst, ngroups,
+                                                                       plan.nsplit, blk, err);
+  else
+    w2tc_kernel<0><<<(unsigned)(batch * ngroups), 128, kSmemW2T, s>>>(mt, my, mw0, mw1, batch, n, K, cfirst, ngroups,
+                                                                       plan.nsplit, blk, err);
   return cudaGetLastError();
 }
 
@@ -1022,11 +1154,11 @@ size_t wide_ws_floats(int64_t batch, int n) {
 int wide_block_launches(int64_t batch, int n, int K, bool update, bool tfactor, bool orgqr) {
   (void)batch;
   (void)K;
-  if (orgqr) return 4;   // vsplit, ygemm, w2build, wupdate
+  if (orgqr) return 4;   // vsplit, ygemm, w2tc, wupdate
   int c = 0;
   if (update || tfactor) c += 2;   // vsplit, ygemm
   if (tfactor) c += 1;             // tbuild
-  if (update) c += 2;              // w2build, wupdate
+  if (update) c += 2;              // w2tc, wupdate
   return c;
 }
 

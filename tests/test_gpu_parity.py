@@ -320,7 +320,7 @@ def test_kernel_timing_report():
     rep = _lib.kernel_timing_report()
     launches = sum(v["launches"] for v in rep.values())
     assert launches == lib.qrb_kernel_launches(4, 512, 1)
-    assert {"panel_kernel", "ygemm_kernel", "wupdate_kernel", "w2build_kernel", "tbuild_kernel"} <= set(rep)
+    assert {"panel_kernel", "ygemm_kernel", "wupdate_kernel", "w2tc_kernel", "tbuild_kernel"} <= set(rep)
     assert all(v["ms"] > 0 for v in rep.values())
     assert _lib.kernel_timing_report() == {}   # the report cleared the log
 
