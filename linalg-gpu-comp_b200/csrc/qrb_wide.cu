@@ -308,7 +308,10 @@ tbuild_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int nc
   float(*X)[129] = reinterpret_cast<float(*)[129]>(smw + 128 * 129);
   float(*S)[33] = reinterpret_cast<float(*)[33]>(smw + 2 * 128 * 129);
   const int tid = threadIdx.x;
-  const int64_t mat = blockIdx.x;
+  // One CTA per (matrix, 32-column block b of T): column block b depends only on the
+  // blocks above it in the same column (T_ab = -T_aa sum_{a<c<=b} G_ac T_cb).
+  const int64_t mat = blockIdx.x >> 2;
+  const int bcol = (int)(blockIdx.x & 3);
   // Gram strip (summed over the row chunks) and the diagonal T blocks, 16 float4 per
   // thread with all loads in flight before the shared-memory stores.
   {
@@ -349,7 +352,7 @@ tbuild_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int nc
   }
   __syncthreads();
   const int ti = tid >> 3, tj = (tid & 7) * 4;
-  for (int b = 1; b < np; ++b) {
+  for (int b = bcol; b == bcol && b < np; ++b) {
     for (int a = b - 1; a >= 0; --a) {
       // S = sum_{c=a+1..b} G_ac X_cb
       float s[4] = {0.f, 0.f, 0.f, 0.f};
@@ -377,11 +380,12 @@ tbuild_kernel(const float* __restrict__ ypart, int nsplit, int64_t batch, int nc
       __syncthreads();
     }
   }
+  // Column block bcol of T (rows 0-127, 32 columns).
   float4* T = reinterpret_cast<float4*>(t128 + (size_t)mat * kWB * kWB);
-#pragma unroll 4
-  for (int k = 0; k < 16; ++k) {
-    const int u = tid + 256 * k, i = u >> 5, j = 4 * (u & 31);
-    T[u] = make_float4(X[i][j], X[i][j + 1], X[i][j + 2], X[i][j + 3]);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int u = tid + 256 * k, i = u >> 3, j = 32 * bcol + 4 * (u & 7);
+    T[i * 32 + (j >> 2)] = make_float4(X[i][j], X[i][j + 1], X[i][j + 2], X[i][j + 3]);
   }
 }
 
@@ -1062,7 +1066,7 @@ cudaError_t run_ygemm(int mode, const float* src, const float* H, const WideWs& 
 cudaError_t run_tbuild(const WideWs& w, const YPlan& plan, const float* t32blk, int np, int blk, int64_t batch,
                        int n, cudaStream_t s) {
   LaunchTimer timer("tbuild_kernel", s, (double)batch * (plan.nsplit + 1) * kWB * kWB * 4.0);
-  tbuild_kernel<<<(unsigned)batch, 256, kSmemT, s>>>(w.ypart, plan.nsplit, batch, ycols(n), t32blk, np,
+  tbuild_kernel<<<(unsigned)(batch * 4), 256, kSmemT, s>>>(w.ypart, plan.nsplit, batch, ycols(n), t32blk, np,
                                                     w.t128 + (size_t)blk * batch * kWB * kWB);
   return cudaGetLastError();
 }
