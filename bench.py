@@ -314,8 +314,10 @@ def bench_config(config: str, args, dist, rank: int, world: int, dev, steps: int
     import qr_b200
     from qr_b200.inputs import CONFIGS, config_input
     batch, n, _ = CONFIGS[config]
+    if config == args.config and args.batch is not None:
+        batch = args.batch
     lo, hi = shard(batch, rank, world)
-    full = config_input(config, seed=args.seed, device=dev)
+    full = config_input(config, seed=args.seed, device=dev, batch=batch)
     A = full[lo:hi].contiguous()
     del full
     H = torch.empty_like(A)
@@ -323,9 +325,14 @@ def bench_config(config: str, args, dist, rank: int, world: int, dev, steps: int
     Q = torch.empty_like(A)
     stream = torch.cuda.current_stream(dev)
 
+    geqrf_only = args.op == "geqrf" and config == args.config
+
     def step():
         if A.shape[0] > 0:
-            qr_b200.qr(A, out=(H, tau, Q))
+            if geqrf_only:
+                qr_b200.geqrf(A, out=(H, tau))
+            else:
+                qr_b200.qr(A, out=(H, tau, Q))
 
     for _ in range(max(warmup, 3)):
         step()
@@ -509,6 +516,10 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="skip the other configurations")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the configuration's batch (profiling captures on a small case)")
+    ap.add_argument("--op", choices=["qr", "geqrf"], default="qr",
+                    help="geqrf: time the factorisation alone (profiling); the metric is defined on qr")
     ap.add_argument("--suite", choices=["gpumode"], default=None,
                     help="gpumode: custom_kernel on the reference task's benchmark shapes (one line each)")
     args = ap.parse_args(argv)

@@ -22,6 +22,7 @@
 #include <cooperative_groups.h>
 
 #include "qrb_internal.cuh"
+#include "qrb_sm100.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -32,7 +33,7 @@ namespace {
 template <int RPT, int CL, int W>
 __global__ void __launch_bounds__(W * 32)
 panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __restrict__ tau,
-             float* __restrict__ Tout, int n, int k, int b) {
+             float* __restrict__ Tout, int n, int k, int b, int* err) {
   constexpr int kPanelWarps = W;
   constexpr int kRowsCta = W * RPT;
   __shared__ float2 red_n[2][W];                  // per-warp (tail^2, alpha) partials
@@ -44,6 +45,7 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   __shared__ float Ts[32][33];                    // T factor (rank 0 only)
   __shared__ float Gt[32][32];                    // Gt[j][c] = (V^T V)[c][j], c < j (rank 0)
   __shared__ float taus[32];
+  __shared__ uint64_t cbar[2];                    // per step parity: the cluster's partials landed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int rank = 0;
@@ -52,6 +54,19 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
   const int m = n - k;
   const size_t moff = (size_t)mat * n * n;
   const int row0 = rank * kRowsCta + warp;        // panel row of register 0
+
+  if constexpr (CL > 1) {
+    if (threadIdx.x == 0) {
+      sm100::mbar_init(&cbar[0], 1);
+      sm100::mbar_init(&cbar[1], 1);
+      sm100::fence_mbar_init();
+    }
+    cg::this_cluster().sync();   // every CTA's barriers exist before anything is pushed to them
+  }
+  // Bytes each CTA receives per step: every CTA's 32 dot partials and (tail, alpha), and
+  // row j of the panel from rank 0.
+  constexpr uint32_t kStepBytes = CL * (32 * 4 + 8) + 32 * 4;
+  bool ok = true;
 
   float a[RPT];
 #pragma unroll
@@ -111,9 +126,13 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
       }
       aj = rowj[par][lane];
     } else {
-      // CTA sums first, then every rank receives all CL of them through distributed
-      // shared memory and adds them in rank order (bit-identical beta / tau everywhere).
-      auto cluster = cg::this_cluster();
+      // CTA sums first; warp 0 pushes them into every rank's receive buffers with
+      // st.async, each store completing its bytes on the receiver's mbarrier, and every
+      // CTA waits on its own barrier only (no cluster-wide barrier per step).  Each CTA
+      // then adds the CL sums in rank order (bit-identical beta / tau everywhere).  The
+      // buffers alternate by step parity: a CTA sends step j + 2 only after it has
+      // received every CTA's step j + 1, which each sends after reading its step-j buffer.
+      if (threadIdx.x == 0) sm100::mbar_arrive_expect_tx(&cbar[par], kStepBytes);
       if (warp == 0) {
         float2 p = make_float2(0.f, 0.f);
         float sw = 0.f;
@@ -124,14 +143,19 @@ panel_kernel(const float* __restrict__ src, float* __restrict__ H, float* __rest
           p.y += t.y;
           sw += red_w[par][q][lane];
         }
+        const float rj = rowj[par][lane];
 #pragma unroll
         for (int q = 0; q < CL; ++q) {
-          *cluster.map_shared_rank(&cred_w[par][rank][lane], q) = sw;
-          if (lane == 0) *cluster.map_shared_rank(&cred_n[par][rank], q) = p;
-          if (rank == 0) *cluster.map_shared_rank(&crowj[par][lane], q) = rowj[par][lane];
+          const uint32_t bar = sm100::mapa_shared(sm100::smem_u32(&cbar[par]), q);
+          sm100::st_async_f32(sm100::mapa_shared(sm100::smem_u32(&cred_w[par][rank][lane]), q), sw, bar);
+          if (lane == 0) sm100::st_async_f32x2(sm100::mapa_shared(sm100::smem_u32(&cred_n[par][rank]), q), p, bar);
+          if (rank == 0) sm100::st_async_f32(sm100::mapa_shared(sm100::smem_u32(&crowj[par][lane]), q), rj, bar);
         }
       }
-      cluster.sync();
+      if (ok && !sm100::mbar_wait(&cbar[par], (j >> 1) & 1)) {
+        ok = false;
+        atomicCAS(err, 0, 70);
+      }
 #pragma unroll
       for (int q = 0; q < CL; ++q) {
         const float2 t = cred_n[par][q];
@@ -230,7 +254,9 @@ cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL, W>, src, H, tau, T, n, k, b);
+  int* err = device_error_flag();
+  if (err == nullptr) return cudaErrorInvalidValue;
+  return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL, W>, src, H, tau, T, n, k, b, err);
 }
 
 }  // namespace
