@@ -220,17 +220,27 @@ int blocked_orgqr(const float* H, float* Q, int64_t batch, int n, void* ws, cuda
 }
 
 // (H, tau[, Q]) of a device batch on stream s; arguments already checked.
-int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+// The QR in two halves: run_qr_h leaves (H, tau) final; run_qr_q forms Q from them
+// (nothing to do for n <= 64, where one launch does both).  The host pipeline copies H
+// out while Q is being formed.
+int run_qr_h(const float* A, float* H, float* tau, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
   if (n <= qrb::kSmallMaxN) {
     QRB_CUDA(qrb::launch_small(A, H, tau, Q, batch, n, Q != nullptr ? 3 : 1, s), "small-n kernel launch");
     return QRB_OK;
   }
-  if (use_wide(n)) {
-    QRB_TRY(wide_geqrf(A, H, tau, batch, n, ws, Q != nullptr, s));
-    return Q != nullptr ? wide_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
-  }
-  QRB_TRY(blocked_geqrf(A, H, tau, batch, n, ws, s));
-  return Q != nullptr ? blocked_orgqr(H, Q, batch, n, ws, s) : QRB_OK;
+  if (use_wide(n)) return wide_geqrf(A, H, tau, batch, n, ws, Q != nullptr, s);
+  return blocked_geqrf(A, H, tau, batch, n, ws, s);
+}
+
+int run_qr_q(const float* H, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  if (Q == nullptr || n <= qrb::kSmallMaxN) return QRB_OK;
+  if (use_wide(n)) return wide_orgqr(H, Q, batch, n, ws, s);
+  return blocked_orgqr(H, Q, batch, n, ws, s);
+}
+
+int run_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n, void* ws, cudaStream_t s) {
+  QRB_TRY(run_qr_h(A, H, tau, Q, batch, n, ws, s));
+  return run_qr_q(H, Q, batch, n, ws, s);
 }
 
 // Kernels run_qr enqueues (it mirrors that dispatch).
@@ -320,7 +330,7 @@ bool pipe_streams(int dev, cudaStream_t (&out)[3]) {
 }
 
 struct Events {
-  cudaEvent_t e[3 * kSlots + 1] = {};
+  cudaEvent_t e[4 * kSlots + 1] = {};
   int made = 0;
   cudaError_t create() {
     for (auto& x : e) {
@@ -348,17 +358,18 @@ int host_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n
   QRB_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   cudaStream_t st[3];
   if (!pipe_streams(dev, st)) return fail(QRB_ERR_CUDA, "could not create the pipeline streams");
-  Events ev;   // [slot]: copied in, computed, copied out; last: fork
+  Events ev;   // [slot]: copied in, computed, copied out, H final; last: fork
   QRB_CUDA(ev.create(), "cudaEventCreate");
   cudaEvent_t* in_ev = ev.e;
   cudaEvent_t* done_ev = ev.e + kSlots;
   cudaEvent_t* out_ev = ev.e + 2 * kSlots;
-  cudaEvent_t fork = ev.e[3 * kSlots];
+  cudaEvent_t* h_ev = ev.e + 3 * kSlots;
+  cudaEvent_t fork = ev.e[4 * kSlots];
   QRB_CUDA(cudaEventRecord(fork, s), "cudaEventRecord");
   for (auto x : st) QRB_CUDA(cudaStreamWaitEvent(x, fork, 0), "cudaStreamWaitEvent");
   const size_t nn = (size_t)n * n;
   int chunk = 0;
-  for (int64_t b0 = 0; b0 < batch; b0 += p.cb, ++chunk) {
+  for (int64_t b0 = 0; b0 < batch; ++chunk) {
     const int64_t cb = batch - b0 < p.cb ? batch - b0 : p.cb;
     const int slot = chunk % kSlots;
     char* base = static_cast<char*>(dws) + slot * p.slot_bytes;
@@ -371,17 +382,22 @@ int host_qr(const float* A, float* H, float* tau, float* Q, int64_t batch, int n
              "copy-in");
     QRB_CUDA(cudaEventRecord(in_ev[slot], st[0]), "cudaEventRecord");
     QRB_CUDA(cudaStreamWaitEvent(st[1], in_ev[slot], 0), "cudaStreamWaitEvent");
-    QRB_TRY(run_qr(X, X, T, Qd, cb, n, W, st[1]));
+    // H and tau go out while Q is formed (the Q kernels only read H).
+    QRB_TRY(run_qr_h(X, X, T, Qd, cb, n, W, st[1]));
+    QRB_CUDA(cudaEventRecord(h_ev[slot], st[1]), "cudaEventRecord");
+    QRB_TRY(run_qr_q(X, Qd, cb, n, W, st[1]));
     QRB_CUDA(cudaEventRecord(done_ev[slot], st[1]), "cudaEventRecord");
-    QRB_CUDA(cudaStreamWaitEvent(st[2], done_ev[slot], 0), "cudaStreamWaitEvent");
+    QRB_CUDA(cudaStreamWaitEvent(st[2], h_ev[slot], 0), "cudaStreamWaitEvent");
     QRB_CUDA(cudaMemcpyAsync(H + b0 * nn, X, cb * nn * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
              "copy-out");
     QRB_CUDA(cudaMemcpyAsync(tau + b0 * n, T, cb * n * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
              "copy-out");
+    QRB_CUDA(cudaStreamWaitEvent(st[2], done_ev[slot], 0), "cudaStreamWaitEvent");
     if (Qd != nullptr)
       QRB_CUDA(cudaMemcpyAsync(Q + b0 * nn, Qd, cb * nn * sizeof(float), cudaMemcpyDeviceToHost, st[2]),
                "copy-out");
     QRB_CUDA(cudaEventRecord(out_ev[slot], st[2]), "cudaEventRecord");
+    b0 += cb;
   }
   // Join: the copy-out stream is downstream of the other two.
   QRB_CUDA(cudaEventRecord(fork, st[2]), "cudaEventRecord");
