@@ -610,8 +610,8 @@ w2tc_kernel(const __grid_constant__ CUtensorMap map_t, const __grid_constant__ C
 // set the pace; a tf32 MMA also costs at least ~44 cycles whatever its N, so N=32
 // strips were MMA-issue-bound.)
 // Warp roles per CTA: 0 = C and V producer, 1 = MMA issuer (leader) and TMEM owner,
-// 2-5 and 7-10 = two epilogue warpgroups taking alternate strips (C -= V W2; the first
-// also splits each item's V tile into the tensor memory), 6 = W2 producer.
+// 2-5 and 7-10 = two epilogue warpgroups taking alternate strips (C -= V W2), 6 = W2
+// producer, 11-14 = V splitter (each item's V tile into the tensor memory).
 // Barriers the MMA waits on live in the leader (W2 landed in both CTAs, both CTAs'
 // epilogues done with an accumulator, both V tiles ready); the leader's commits arrive
 // in both CTAs.
@@ -630,11 +630,11 @@ constexpr uint32_t kUOffW = kUOffV + 4 * kUCBox;
 constexpr uint32_t kUOffC = kUOffW + kUWSlots * kUWSlot;
 constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUCSlot;
 constexpr uint32_t kSmemU = kUBarOff + 512 + 1024;
-constexpr int kUThreads = 352;
+constexpr int kUThreads = 480;
 
 struct UBars {
   uint64_t cfull[kUCSlots], cempty[kUCSlots], wfull[kUWSlots], wempty[kUWSlots], vfull, vempty, vready,
-      accf[kUAcc], acce[kUAcc], drain;
+      accf[kUAcc], acce[kUAcc], drain, vdone;
   uint32_t tmem;
   int abort;
 };
@@ -691,6 +691,7 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       mbar_init(&bars.acce[i], 8);   // both CTAs' epilogue warps (leader's copy is used)
     }
     mbar_init(&bars.drain, 1);
+    mbar_init(&bars.vdone, 1);
     bars.abort = 0;
     fence_mbar_init();
   }
@@ -814,6 +815,7 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
           mma_commit_pair(&bars.wempty[slot]);
           issued = true;
         }
+        if (!stop) mma_commit_pair(&bars.vdone);   // the item's MMAs no longer read V
       }
       if (*abort) {
         if (issued) {   // tensor memory must not be released under running MMAs
@@ -824,23 +826,21 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
           if (w_last[sl] >= 0) mbar_wait(&bars.wfull[sl], w_last[sl] & 1, 1u << 22);
       }
     }
-  } else {
-    // ---------------- epilogue warpgroups (warps 2-5: wg 0, 7-10: wg 1) ----------------
-    const int wg = warp >= 7 ? 1 : 0;
+  } else if (warp >= 11) {
+    // ---------------- V splitter (warps 11-14) ----------------
+    // V rows of this CTA, masked to the unit lower trapezoid, split into the tensor memory
+    // once the previous item's MMAs have completed (`vdone`, committed once per item: one
+    // phase per item, and the MMAs of item i + 1 wait for this split, so the wait is never
+    // more than one phase behind).  A warpgroup of its own, so that the next item's MMAs
+    // wait only for the split, not for an epilogue warpgroup to finish its last strip.
     const int q = warp & 3;
     const int r = 32 * q + lane;   // row within this CTA's 128 = TMEM lane
     const uint32_t tl = (uint32_t)(32 * q) << 16;
-    int gs = 0, iter = 0;
-    bool stop = false;
-    for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
+    int iter = 0;
+    for (int64_t item = pair; item < nitems; item += npairs, ++iter) {
       const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
-      const int y = it.y0 + rowoff;
-      const int R = y + r;
-      if (wg == 0) {
-      // V rows of this CTA, masked to the unit lower trapezoid, split into the tensor
-      // memory once the previous item's MMAs have completed (the accumulator of its
-      // last strip, whichever warpgroup reads it, has been written).
-      if (gs > 0 && !wwait(&bars.accf[(gs - 1) % kUAcc], ((gs - 1) / kUAcc) & 1, abort, err, 51)) break;
+      const int R = it.y0 + rowoff + r;
+      if (iter > 0 && !wwait(&bars.vdone, (iter - 1) & 1, abort, err, 51)) break;
       if (!wwait(&bars.vfull, iter & 1, abort, err, 46)) break;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -864,7 +864,19 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
         mbar_arrive(&bars.vempty);               // staging free for the next item's V
         mbar_arrive_cluster(lead_vready);        // this CTA's quarter of V is in TMEM
       }
-      }
+    }
+  } else {
+    // ---------------- epilogue warpgroups (warps 2-5: wg 0, 7-10: wg 1) ----------------
+    const int wg = warp >= 7 ? 1 : 0;
+    const int q = warp & 3;
+    const int r = 32 * q + lane;   // row within this CTA's 128 = TMEM lane
+    const uint32_t tl = (uint32_t)(32 * q) << 16;
+    int gs = 0, iter = 0;
+    bool stop = false;
+    for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
+      const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
+      const int y = it.y0 + rowoff;
+      const int R = y + r;
       for (int s = it.s0; s < it.s1; ++s, ++gs) {
         if ((gs & 1) != wg) continue;
         const int slot = gs % kUCSlots, acc = gs % kUAcc;
