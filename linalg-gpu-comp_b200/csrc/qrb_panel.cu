@@ -279,7 +279,12 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T, int64
   if (m <= 256) return launch_panel_t<32, 1>(src, H, tau, T, batch, n, k, b, s);
   if (m <= 512) return launch_panel_t<64, 1>(src, H, tau, T, batch, n, k, b, s);
   if (m <= 1024) return launch_panel_t<32, 4>(src, H, tau, T, batch, n, k, b, s);
-  if (m <= 2048) return launch_panel_t<32, 8>(src, H, tau, T, batch, n, k, b, s);
+  // 1024 < m <= 2048: with 16+ matrices the GPU is full either way, and 4-CTA clusters of
+  // 512 rows cost less per column than 8-CTA clusters of 256 (cheaper exchange; measured
+  // b32_n2048 panels 2.70 vs 2.90 ms); a small batch keeps the 8-CTA spread (b8_n2048
+  // 6.14 vs 6.27 ms, b2_n4096 13.99 vs 14.13 ms).
+  if (m <= 2048) return batch >= 16 ? launch_panel_t<64, 4>(src, H, tau, T, batch, n, k, b, s)
+                                    : launch_panel_t<32, 8>(src, H, tau, T, batch, n, k, b, s);
   return launch_panel_t<64, 8>(src, H, tau, T, batch, n, k, b, s);
 }
 
