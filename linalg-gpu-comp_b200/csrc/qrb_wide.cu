@@ -615,17 +615,16 @@ w2tc_kernel(const __grid_constant__ CUtensorMap map_t, const __grid_constant__ C
 // Barriers the MMA waits on live in the leader (W2 landed in both CTAs, both CTAs'
 // epilogues done with an accumulator, both V tiles ready); the leader's commits arrive
 // in both CTAs.
-constexpr int kUCSlots = 3;
-constexpr int kUWSlots = 2;
-constexpr int kUAcc = 4;
-constexpr int kUTN = 64;                           // strip width (N of the pair MMA)
+constexpr int kUCSlots = 3;                        // half-strips of C (64 columns)
+constexpr int kUWSlots = 4;                        // W2 chunks (K = 32)
+constexpr int kUAcc = 2;
+constexpr int kUTN = 128;                          // strip width (N of the pair MMA)
 constexpr int kUHalf = kUTN / 2;                   // W2 columns each CTA holds
 constexpr uint32_t kUCBox = 128 * 128;             // 128 rows x 32 fp32
-constexpr uint32_t kUCSlot = 2 * kUCBox;           // one C strip: 128 rows x 64 columns
+constexpr uint32_t kUCSlot = 2 * kUCBox;           // one C half-strip: 128 rows x 64 columns
 constexpr uint32_t kUOffV = 0;                     // V staging: 4 boxes of 128 rows x 32
-constexpr uint32_t kUWBox = kUHalf * 128;          // 32 columns x 32 K values
-constexpr uint32_t kUWPiece = 4 * kUWBox;          // K = 128
-constexpr uint32_t kUWSlot = 2 * kUWPiece;         // two tf32 pieces (16 KB each)
+constexpr uint32_t kUWPiece = kUHalf * 128;        // 64 strip columns x 32 K values (8 KB)
+constexpr uint32_t kUWSlot = 2 * kUWPiece;         // one K chunk, two tf32 pieces
 constexpr uint32_t kUOffW = kUOffV + 4 * kUCBox;
 constexpr uint32_t kUOffC = kUOffW + kUWSlots * kUWSlot;
 constexpr uint32_t kUBarOff = kUOffC + kUCSlots * kUCSlot;
@@ -725,7 +724,7 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 4; ++j) tma_load_3d(sm + kUOffV + j * kUCBox, &map_v, K + 32 * j, y, it.mat, &bars.vfull);
         v_last = iter;
-        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        for (int hs = 2 * it.s0; hs < 2 * it.s1; ++hs, ++gs) {   // half-strips
           const int slot = gs % kUCSlots, use = gs / kUCSlots;
           if (use > 0 && !wwait(&bars.cempty[slot], (use - 1) & 1, abort, err, 42)) {
             stop = true;
@@ -733,8 +732,8 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
           }
           mbar_arrive_expect_tx(&bars.cfull[slot], kUCSlot);
           unsigned char* cb = sm + kUOffC + slot * kUCSlot;
-          tma_load_3d(cb, &map_src, c0 + s * kUTN, y, it.mat, &bars.cfull[slot]);
-          tma_load_3d(cb + kUCBox, &map_src, c0 + s * kUTN + 32, y, it.mat, &bars.cfull[slot]);
+          tma_load_3d(cb, &map_src, c0 + hs * 64, y, it.mat, &bars.cfull[slot]);
+          tma_load_3d(cb + kUCBox, &map_src, c0 + hs * 64 + 32, y, it.mat, &bars.cfull[slot]);
           last_use[slot] = use;
         }
       }
@@ -756,22 +755,19 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       bool stop = false;
       for (int64_t item = pair; item < nitems && !stop; item += npairs) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
-        for (int s = it.s0; s < it.s1; ++s, ++gs) {
+        for (int cidx = 4 * it.s0; cidx < 4 * it.s1; ++cidx, ++gs) {   // K chunks of strips
           const int slot = gs % kUWSlots, use = gs / kUWSlots;
           if (use > 0 && !wwait(&bars.wempty[slot], (use - 1) & 1, abort, err, 50)) {
             stop = true;
             break;
           }
           unsigned char* sl = sm + kUOffW + slot * kUWSlot;
-          const int cs = c0 + s * kUTN + kUHalf * (int)rank;
+          const int cs = c0 + (cidx >> 2) * kUTN + kUHalf * (int)rank, kc = cidx & 3;
           const uint32_t bar = lead_wfull0 + slot * (uint32_t)sizeof(uint64_t);
           // The leader expects both halves' bytes; the peer's copies count on the leader's barrier.
           if (leader) mbar_arrive_expect_tx(&bars.wfull[slot], 2 * kUWSlot);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            tma_load_3d_pair(sl + j * kUWBox, &map_w0, 32 * j, cs, it.mat, bar);
-            tma_load_3d_pair(sl + kUWPiece + j * kUWBox, &map_w1, 32 * j, cs, it.mat, bar);
-          }
+          tma_load_3d_pair(sl, &map_w0, 32 * kc, cs, it.mat, bar);
+          tma_load_3d_pair(sl + kUWPiece, &map_w1, 32 * kc, cs, it.mat, bar);
           last_use[slot] = use;
         }
       }
@@ -781,7 +777,7 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
     // ---------------- MMA issuer (leader only) ----------------
     if (lane == 0 && leader) {
       constexpr uint32_t idesc = idesc_tf32(256, kUTN, 0, 0);
-      int gs = 0, iter = 0;
+      int gs = 0, gc = 0, iter = 0;
       bool issued = false, stop = false;
       int w_last[kUWSlots];
 #pragma unroll
@@ -789,31 +785,46 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       for (int64_t item = pair; item < nitems && !stop; item += npairs, ++iter) {
         const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
         if (!wwait(&bars.vready, iter & 1, abort, err, 43)) break;
-        for (int s = it.s0; s < it.s1; ++s, ++gs) {
-          const int slot = gs % kUWSlots, acc = gs % kUAcc;
-          w_last[slot] = gs / kUWSlots;
-          if (!wwait(&bars.wfull[slot], (gs / kUWSlots) & 1, abort, err, 44) ||
-              (gs >= kUAcc && !wwait(&bars.acce[acc], ((gs / kUAcc) - 1) & 1, abort, err, 45))) {
+        for (int s = it.s0; s < it.s1 && !stop; ++s, ++gs) {
+          const int acc = gs % kUAcc;
+          if (gs >= kUAcc && !wwait(&bars.acce[acc], ((gs / kUAcc) - 1) & 1, abort, err, 45)) {
             stop = true;
             break;
           }
-          tc_fence_after();
-          const uint32_t wb = smem_u32(sm + kUOffW + slot * kUWSlot);
           const uint32_t d = tmem + kAcc + acc * kUTN;
+          // The strip's four K chunks stay resident: the two small products of every chunk
+          // go in first, then the hi x hi products, releasing each chunk after its last use
+          // (the small terms accumulate before the large ones over the whole K, as in one
+          // K = 128 chain; chunk-by-chunk order measurably loses accuracy).
+          for (int pass = 0; pass < 2 && !stop; ++pass) {
+            for (int kc = 0; kc < 4; ++kc) {
+              const int g = gc + kc, slot = g % kUWSlots;
+              if (pass == 0) {
+                w_last[slot] = g / kUWSlots;
+                if (!wwait(&bars.wfull[slot], (g / kUWSlots) & 1, abort, err, 44)) {
+                  stop = true;
+                  break;
+                }
+                tc_fence_after();
+              }
+              const uint32_t wb = smem_u32(sm + kUOffW + slot * kUWSlot);
 #pragma unroll
-          for (int tt = 0; tt < 3; ++tt) {
+              for (int tt = 0; tt < 3; ++tt) {
+                if ((tt == 2) != (pass == 1)) continue;
 #pragma unroll
-            for (int kk = 0; kk < 16; ++kk) {
-              const uint32_t a = tmem + kWTermA[tt] * 128 + kk * 8;
-              // Each CTA's half: 32 rows (strip columns) x 32 K values per box, K-major.
-              const uint64_t bd =
-                  sdesc_sw128(wb + kWTermB[tt] * kUWPiece + (kk >> 2) * kUWBox + (kk & 3) * 32, 16, 1024);
-              mma_tf32_ta_pair(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
+                for (int k4 = 0; k4 < 4; ++k4) {
+                  const uint32_t a = tmem + kWTermA[tt] * 128 + (4 * kc + k4) * 8;
+                  // Each CTA's half: 64 rows (strip columns) x 32 K values, K-major.
+                  const uint64_t bd = sdesc_sw128(wb + kWTermB[tt] * kUWPiece + k4 * 32, 16, 1024);
+                  mma_tf32_ta_pair(d, a, bd, idesc, (pass > 0 || kc > 0 || tt > 0 || k4 > 0) ? 1u : 0u);
+                }
+              }
+              if (pass == 1) mma_commit_pair(&bars.wempty[slot]);
+              issued = true;
             }
           }
-          mma_commit_pair(&bars.accf[acc]);
-          mma_commit_pair(&bars.wempty[slot]);
-          issued = true;
+          gc += 4;
+          if (!stop) mma_commit_pair(&bars.accf[acc]);
         }
         if (!stop) mma_commit_pair(&bars.vdone);   // the item's MMAs no longer read V
       }
@@ -877,64 +888,73 @@ wupdate_kernel(const __grid_constant__ CUtensorMap map_v, const __grid_constant_
       const UItem it = u_item(item, K, ntiles, ngroups, gsize, nstrips);
       const int y = it.y0 + rowoff;
       const int R = y + r;
-      for (int s = it.s0; s < it.s1; ++s, ++gs) {
+      for (int s = it.s0; s < it.s1 && !stop; ++s, ++gs) {
         if ((gs & 1) != wg) continue;
-        const int slot = gs % kUCSlots, acc = gs % kUAcc;
-        const int cs = c0 + s * kUTN;
-        unsigned char* cbox = sm + kUOffC + slot * kUCSlot;
-        if (!wwait(&bars.cfull[slot], (gs / kUCSlots) & 1, abort, err, 47) ||
-            !wwait(&bars.accf[acc], (gs / kUAcc) & 1, abort, err, 48)) {
+        const int acc = gs % kUAcc;
+        if (!wwait(&bars.accf[acc], (gs / kUAcc) & 1, abort, err, 48)) {
           stop = true;
           break;
         }
         tc_fence_after();
-        float d[2][32];
-        tmem_ld32(tmem + tl + kAcc + acc * kUTN, d[0]);
-        tmem_ld32(tmem + tl + kAcc + acc * kUTN + 32, d[1]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(lead_acce0 + acc * (uint32_t)sizeof(uint64_t));
-        // Row R of the strip: C - V W2 is written back in place into the slot, then the
-        // warp stores its 32 rows to global memory coalesced (lanes 0-15 and 16-31 each
-        // cover one 256-byte row per instruction).
+        // Two 64-column halves, each in its own C slot (half-strip 2 gs + h2).
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const int hs = 2 * gs + h2, slot = hs % kUCSlots;
+          const int cs = c0 + s * kUTN + 64 * h2;
+          unsigned char* cbox = sm + kUOffC + slot * kUCSlot;
+          if (!wwait(&bars.cfull[slot], (hs / kUCSlots) & 1, abort, err, 47)) {
+            stop = true;
+            break;
+          }
+          float d[2][32];
+          tmem_ld32(tmem + tl + kAcc + acc * kUTN + 64 * h2, d[0]);
+          tmem_ld32(tmem + tl + kAcc + acc * kUTN + 64 * h2 + 32, d[1]);
+          if (h2 == 1) {   // the accumulator is free once its second half is read
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(lead_acce0 + acc * (uint32_t)sizeof(uint64_t));
+          }
+          // Row R of the half-strip: C - V W2 is written back in place into the slot, then
+          // the warp stores its 32 rows to global memory coalesced (lanes 0-15 and 16-31
+          // each cover one 256-byte row per instruction).
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int qq = 0; qq < 8; ++qq) {
-            float4* cp = reinterpret_cast<float4*>(cbox + h * kUCBox + off128_w(r, qq));
-            const float4 cv4 = *cp;
-            float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
+            for (int qq = 0; qq < 8; ++qq) {
+              float4* cp = reinterpret_cast<float4*>(cbox + h * kUCBox + off128_w(r, qq));
+              const float4 cv4 = *cp;
+              float cv[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              if constexpr (IDENT) {
-                const int Cc = cs + 32 * h + 4 * qq + e;
-                if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+              for (int e = 0; e < 4; ++e) {
+                if constexpr (IDENT) {
+                  const int Cc = cs + 32 * h + 4 * qq + e;
+                  if (R < n && Cc < n && (R < kb || Cc < kb)) cv[e] = R == Cc ? 1.f : 0.f;
+                }
+                cv[e] -= d[h][4 * qq + e];
               }
-              cv[e] -= d[h][4 * qq + e];
+              *cp = make_float4(cv[0], cv[1], cv[2], cv[3]);
             }
-            *cp = make_float4(cv[0], cv[1], cv[2], cv[3]);
           }
-        }
-        __syncwarp();
-        {
-          const int sub = lane >> 4, q4 = lane & 15;   // row parity, float4 column 0..15
-          const int h = q4 >> 3, qq = q4 & 7;
+          __syncwarp();
+          {
+            const int sub = lane >> 4, q4 = lane & 15;   // row parity, float4 column 0..15
+            const int h = q4 >> 3, qq = q4 & 7;
 #pragma unroll 4
-          for (int i = 0; i < 16; ++i) {
-            const int rr = 32 * q + 2 * i + sub;       // tile row written by this lane
-            const int Rg = y + rr;
-            const float4 v = *reinterpret_cast<const float4*>(cbox + h * kUCBox + off128_w(rr, qq));
-            if (Rg < n && cs + 4 * q4 < n)
-              *reinterpret_cast<float4*>(dst + ((size_t)it.mat * n + Rg) * n + cs + 4 * q4) = v;
+            for (int i = 0; i < 16; ++i) {
+              const int rr = 32 * q + 2 * i + sub;       // tile row written by this lane
+              const int Rg = y + rr;
+              const float4 v = *reinterpret_cast<const float4*>(cbox + h * kUCBox + off128_w(rr, qq));
+              if (Rg < n && cs + 4 * q4 < n)
+                *reinterpret_cast<float4*>(dst + ((size_t)it.mat * n + Rg) * n + cs + 4 * q4) = v;
+            }
           }
+          // Release the slot only after this warp's reads of it have completed (their values
+          // are consumed by the stores above) and are ordered before the TMA (async proxy)
+          // that refills it; releasing right after issuing the loads let a slow warp read
+          // the next strip's data.
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bars.cempty[slot]);
         }
-        // Release the slot only after this warp's reads of it have completed (their values
-        // are consumed by the stores above) and are ordered before the TMA (async proxy)
-        // that refills it; releasing right after issuing the loads let a slow warp read
-        // the next strip's data.
-        fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&bars.cempty[slot]);
       }
     }
   }
