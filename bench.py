@@ -76,15 +76,23 @@ def shard(batch: int, rank: int, world: int) -> tuple[int, int]:
     return rank * batch // world, (rank + 1) * batch // world
 
 
-def load_traffic(config: str):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+def load_traffic(config: str) -> dict:
+    """Per-kernel DRAM traffic of a configuration from the committed ncu summaries: either
+    bytes per launch, or DRAM bytes per algorithmic byte measured on a smaller case of the
+    same kernel (scaled by the run's algorithmic bytes per launch)."""
     p = ROOT / "profiles" / "traffic.json"
     if p.exists():
-        d = json.loads(p.read_text())
-        e = d.get(config)
-        if e:
-            return e.get("dram_bytes_per_launch")
-    return None
+        return json.loads(p.read_text()).get(config) or {}
+    return {}
+
+
+def traffic_for(traffic: dict, kernel: str, bytes_per_launch: float):
+    e = (traffic or {}).get(kernel)
+    if not e:
+        return None
+    if "dram_bytes_per_launch" in e:
+        return e["dram_bytes_per_launch"]
+    return e["dram_per_algorithmic"] * bytes_per_launch
 
 
 # ---------------------------------------------------------------------------
@@ -302,7 +310,7 @@ def roofline_from_profile(prof: dict, steps: int, step_ms: float, n: int, batch:
     step_tflops = batch * flops_per_matrix(n) / (step_ms / 1e3) / 1e12
     return {
         "bound": "hbm", "achieved": gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": gbs / peaks["hbm_gbs"], "traffic": traffic, "kernel": name,
+        "frac": gbs / peaks["hbm_gbs"], "traffic": traffic_for(traffic, name, bytes_per_launch), "kernel": name,
         "launches_per_step": d["launches"] / steps, "ms_per_launch": per_launch_ms,
         "algorithmic_bytes_per_launch": bytes_per_launch,
         "share_of_kernel_time": d["ms"] / total if total > 0 else None,

@@ -156,11 +156,12 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
     bars.abort = 0;
     fence_mbar_init();
   }
-  if (warp == 1) tmem_alloc(&bars.tmem, 256);
+  if (warp == 1) tmem_alloc(&bars.tmem, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bars.tmem;
+  constexpr uint32_t kYA = 256;   // A (C^T pieces) per stage: columns kYA + 64 st (piece 0), + 32 (piece 1)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -193,7 +194,7 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_tf32(128, 128, 1, 1);
+      constexpr uint32_t idesc = idesc_tf32(128, 128, 0, 1);   // A from tensor memory, B MN-major
       bool issued = false;
       for (int s = 0; s < nst; ++s) {
         const int st = s % kYStages, acc = s & 1;
@@ -206,9 +207,9 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
         for (int tt = 0; tt < 3; ++tt) {
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t ad = sdesc_sw128_32b(base + kWTermA[tt] * kYPiece + kk * 1024, kYBox, 512);
+            const uint32_t a = tmem + kYA + 64 * st + 32 * kWTermA[tt] + 8 * kk;
             const uint64_t bd = sdesc_sw128_32b(base + kYOffV + kWTermB[tt] * kYPiece + kk * 1024, kYBox, 512);
-            mma_tf32(d, ad, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
+            mma_tf32_ta(d, a, bd, idesc, (tt > 0 || kk > 0) ? 1u : 0u);
           }
         }
         mma_commit(&bars.accf[acc]);
@@ -221,38 +222,37 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
       }
     }
   } else if (warp < 6) {
-    // ---------------- converters: split the C stage into tf32 pieces ----------------
-    const int ct = tid - 64;
+    // ---------------- converters: C^T pieces into the tensor memory ----------------
+    // Thread = strip column c = TMEM lane (warp w writes lanes 32 (w % 4)..): its 32 rows
+    // of the stage, split into two tf32 pieces, become K columns of the A operand.  Taking
+    // A from the tensor memory halves the MMAs' shared-memory reads, and the split pieces
+    // are no longer written back to shared memory: the stage loop was bound by shared-
+    // memory bandwidth (TMA writes, converter traffic and both MMA operands).
+    const int qd = warp & 3;
+    const int c = 32 * qd + lane;
+    const uint32_t tl = (uint32_t)(32 * qd) << 16;
+    const int Cc = cs + c;
     for (int s = 0; s < nst; ++s) {
       const int st = s % kYStages;
       if (!wwait(&bars.full[st], (s / kYStages) & 1, abort, err, 34)) break;
-      unsigned char* sb = sm + st * kYStage;
+      const unsigned char* p0 = sm + st * kYStage + (c >> 5) * kYBox + (c & 3) * 4;
       const int y = r0 + s * 32;
-#pragma unroll 2
-      for (int i = 0; i < 8; ++i) {
-        const int u = ct + 128 * i;
-        const int box = u >> 8, r = (u >> 3) & 31, q = u & 7;
-        const uint32_t off = off32b_w(r, q);
-        unsigned char* p0 = sb + box * kYBox;
-        float4 v = *reinterpret_cast<float4*>(p0 + off);
-        float a[4] = {v.x, v.y, v.z, v.w};
+      float x0[32], x1[32];
+#pragma unroll
+      for (int r = 0; r < 32; ++r) {
+        float a = *reinterpret_cast<const float*>(p0 + off32b_w(r, (c & 31) >> 2));
         const int R = y + r;
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int Cc = cs + 32 * box + 4 * q + e;
-          if (MODE == 0) {
-            if (gram) a[e] = vmask_w(a[e], R - K, Cc - K, bw);
-          } else {
-            if (R < n && Cc < n && (R < kb || Cc < kb)) a[e] = R == Cc ? 1.f : 0.f;
-          }
+        if (MODE == 0) {
+          if (gram) a = vmask_w(a, R - K, Cc - K, bw);
+        } else {
+          if (R < n && Cc < n && (R < kb || Cc < kb)) a = R == Cc ? 1.f : 0.f;
         }
-        float x0[4], x1[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) split2_tf32(a[e], x0[e], x1[e]);
-        *reinterpret_cast<float4*>(p0 + off) = make_float4(x0[0], x0[1], x0[2], x0[3]);
-        *reinterpret_cast<float4*>(p0 + kYPiece + off) = make_float4(x1[0], x1[1], x1[2], x1[3]);
+        split2_tf32(a, x0[r], x1[r]);
       }
-      fence_proxy_async();
+      tmem_st32(tmem + tl + kYA + 64 * st, x0);
+      tmem_st32(tmem + tl + kYA + 64 * st + 32, x1);
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bars.split[st]);
     }
@@ -293,7 +293,7 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -1084,7 +1084,10 @@ cudaError_t run_ygemm(int mode, const float* src, const float* H, const WideWs& 
     return cudaErrorInvalidValue;
   const unsigned grid = (unsigned)((int64_t)plan.nstrips * batch * plan.nsplit);
   const double m = n - K, nc = cend - K;
-  LaunchTimer timer("ygemm_kernel", s, (double)batch * (4.0 * m * nc + 8.0 * m * kWB * plan.nstrips),
+  // Algorithmic bytes: C once, the V pieces once, the Y partials written (the V pieces
+  // are read again for every strip, but from L2).
+  LaunchTimer timer("ygemm_kernel", s,
+                    (double)batch * (4.0 * m * nc + 8.0 * m * kWB + 4.0 * plan.nsplit * nc * kWB),
                     (double)batch * 2.0 * m * nc * kWB);
   if (mode == 0)
     ygemm_kernel<0><<<grid, kYThreads, kSmemY, s>>>(mc, mh, mv0, mv1, w.ypart, batch, n, K, bw, plan.nstrips,
