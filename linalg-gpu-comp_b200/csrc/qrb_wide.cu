@@ -101,11 +101,11 @@ vsplit_kernel(const float* __restrict__ H, float* __restrict__ vp0, float* __res
 }
 
 // ---- ygemm: Y = C^T V over a row chunk, per 128-column strip ---------------------------
-constexpr int kYStages = 3;
+constexpr int kYStages = 4;
 constexpr uint32_t kYBox = 32 * 128;          // 32 rows x 32 fp32
 constexpr uint32_t kYPiece = 4 * kYBox;       // 32 rows x 128 columns
-constexpr uint32_t kYStage = 4 * kYPiece;     // C pieces 0, 1, then V pieces 0, 1
-constexpr uint32_t kYOffV = 2 * kYPiece;
+constexpr uint32_t kYStage = 3 * kYPiece;     // C (raw), then V pieces 0, 1
+constexpr uint32_t kYOffV = kYPiece;
 constexpr uint32_t kYBarOff = kYStages * kYStage;
 constexpr uint32_t kSmemY = kYBarOff + 256 + 1024;
 constexpr int kYThreads = 320;   // producer, MMA, 4 converter warps, 4 gather warps
@@ -170,7 +170,7 @@ ygemm_kernel(const __grid_constant__ CUtensorMap map_c, const __grid_constant__ 
       prefetch_tensormap(cmap);
       prefetch_tensormap(&map_v0);
       prefetch_tensormap(&map_v1);
-      int last_use[kYStages] = {-1, -1, -1};
+      int last_use[kYStages] = {-1, -1, -1, -1};
       for (int s = 0; s < nst; ++s) {
         const int st = s % kYStages, use = s / kYStages;
         if (use > 0 && !wwait(&bars.sfree[st], (use - 1) & 1, abort, err, 31)) break;
