@@ -345,12 +345,26 @@ w2_kernel(const float* __restrict__ part, const float* __restrict__ Tg, float* _
     if (trans_t) Tt[r][c] = t;        // op(T) = T^T: op(T)[c][r] = T[r][c] -> Tt[r][c]
     else Tt[c][r] = t;                // op(T) = T:   op(T)[r][c] = T[r][c] -> Tt[c][r]
   }
-  for (int idx = threadIdx.x; idx < kTN * 32; idx += blockDim.x) {
-    const int i = idx >> 5, j = idx & 31;
-    float w = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp)
-      w += __ldg(part + ((((size_t)sp * batch + mat) * nstrips + strip) * kTN + i) * 32 + j);
-    Ws[i][j] = w;
+  // Each thread sums 8 elements over the chunks (in chunk order); the 8 loads of a chunk
+  // are independent, so they are in flight together.
+  constexpr int kPer = kTN * 32 / 256;
+  static_assert(kPer == 8, "w2_kernel: 256 threads, 8 elements each");
+  float w[kPer];
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) w[e] = 0.f;
+#pragma unroll 2
+  for (int sp = 0; sp < nsplit; ++sp) {
+    const float* src = part + (((size_t)sp * batch + mat) * nstrips + strip) * kTN * 32;
+    float v[kPer];
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) v[e] = __ldg(src + threadIdx.x + 256 * e);
+#pragma unroll
+    for (int e = 0; e < kPer; ++e) w[e] += v[e];
+  }
+#pragma unroll
+  for (int e = 0; e < kPer; ++e) {
+    const int idx = threadIdx.x + 256 * e;
+    Ws[idx >> 5][idx & 31] = w[e];
   }
   __syncthreads();
   // Thread: strip columns i0, i0 + 32 and reflectors a0..a0+3 (8 outputs, register tile).
