@@ -1064,7 +1064,7 @@ bool set_smem_attrs() {
 cudaError_t run_vsplit(const float* H, const WideWs& w, int64_t batch, int n, int K, int bw, cudaStream_t s) {
   const int64_t units = batch * (int64_t)(n - K) * 32;
   int64_t blocks = (units + 255) / 256;
-  const int64_t cap = 8 * (int64_t)sm_count();
+  const int64_t cap = 64 * (int64_t)sm_count();   // about one unit per thread: every load in flight at once
   if (blocks > cap) blocks = cap;
   LaunchTimer timer("vsplit_kernel", s, (double)batch * (n - K) * (4.0 * bw + 8.0 * kWB));
   vsplit_kernel<<<(unsigned)blocks, 256, 0, s>>>(H, w.vp0, w.vp1, n, K, bw, units);
