@@ -49,7 +49,7 @@ enum qrb_status {
   QRB_ERR_DEVICE = 5         /* current device is not an sm_100 (B200-class) GPU */
 };
 
-#define QRB_MAX_N 4096
+#define QRB_MAX_N 8192
 
 /* Library version, major*10000 + minor*100 + patch. */
 QRB_API int qrb_version(void);

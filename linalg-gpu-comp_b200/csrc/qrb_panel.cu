@@ -19,6 +19,7 @@
 // For c < j the reduced w_c equals (V^T V)[c, j], so the Gram matrix of the T
 // recurrence T[:j, j] = -tau_j T[:j, :j] G[:j, j] (submissions/v1.py:48-56) falls out
 // of the same pass; warp 0 evaluates the recurrence row-parallel after the loop.
+#include <atomic>
 #include <cooperative_groups.h>
 
 #include "qrb_internal.cuh"
@@ -254,6 +255,18 @@ cudaError_t launch_panel_t(const float* src, float* H, float* tau, float* T, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if constexpr (CL > 8) {   // 16-CTA clusters exceed the portable size: opt in once per device
+    static std::atomic<unsigned long long> done{0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return cudaErrorInvalidDevice;
+    const unsigned long long bit = 1ull << (dev & 63);
+    if ((done.load(std::memory_order_acquire) & bit) == 0) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(panel_kernel<RPT, CL, W>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+      done.fetch_or(bit, std::memory_order_acq_rel);
+    }
+  }
   int* err = device_error_flag();
   if (err == nullptr) return cudaErrorInvalidValue;
   return cudaLaunchKernelEx(&cfg, panel_kernel<RPT, CL, W>, src, H, tau, T, n, k, b, err);
@@ -266,7 +279,7 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T, int64
   if (batch == 0) return cudaSuccess;
   const int m = n - k;
   // Single CTA while the panel fits 8 warps x 64 rows; clusters of 256-row CTAs
-  // (512-row for m > 2048) beyond that.
+  // (512-row for m > 2048, 16 of them for m > 4096) beyond that.
   // Short panels: with many matrices in flight (throughput-bound) fewer warps with more
   // rows each cost less per column (fewer partials, cheaper barrier); a small batch is
   // latency-bound and does better spread over 8 warps.  Measured on one B200: b512_n256
@@ -285,7 +298,8 @@ cudaError_t launch_panel(const float* src, float* H, float* tau, float* T, int64
   // 6.14 vs 6.27 ms, b2_n4096 13.99 vs 14.13 ms).
   if (m <= 2048) return batch >= 16 ? launch_panel_t<64, 4>(src, H, tau, T, batch, n, k, b, s)
                                     : launch_panel_t<32, 8>(src, H, tau, T, batch, n, k, b, s);
-  return launch_panel_t<64, 8>(src, H, tau, T, batch, n, k, b, s);
+  if (m <= 4096) return launch_panel_t<64, 8>(src, H, tau, T, batch, n, k, b, s);
+  return launch_panel_t<64, 16>(src, H, tau, T, batch, n, k, b, s);   // up to 8192 rows
 }
 
 }  // namespace qrb

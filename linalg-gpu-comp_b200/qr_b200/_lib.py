@@ -17,7 +17,7 @@ QRB_ERR_UNSUPPORTED = 2
 QRB_ERR_WORKSPACE = 3
 QRB_ERR_CUDA = 4
 QRB_ERR_DEVICE = 5
-QRB_MAX_N = 4096
+QRB_MAX_N = 8192
 
 # name -> (restype, argtypes); mirrors include/qrb200.h one to one.
 _c_int64, _c_size, _vp, _fp = ctypes.c_int64, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p

@@ -84,7 +84,7 @@ def _ws(batch, n):
     (3, 100, 4 * 3 * 4096 + (3 * 100 * 32 + 8 * 3 * 128 * 32) * 4),
     # n >= 256, n % 4 == 0: plus the wide-block scratch
     (7, 512, _ws(7, 512)), (32, 2048, _ws(32, 2048)), (2, 260, _ws(2, 260)), (2, 258, _ws(2, 258)),
-    (1, 4097, 0), (-1, 100, 0)])
+    (1, 4097, _ws(1, 4097)), (1, 8192, _ws(1, 8192)), (1, 8193, 0), (-1, 100, 0)])
 def test_workspace_size(lib, batch, n, expect):
     assert lib.qrb_workspace_size(batch, n) == expect
 
@@ -112,7 +112,7 @@ def test_argument_errors_are_statuses(lib):
     # bad sizes
     assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 0, None, 0, None) == 1
     assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, -1, 8, None, 0, None) == 1
-    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 5000, None, 0, None) == 2
+    assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 8200, None, 0, None) == 2
     assert "QRB_MAX_N" in _err(lib)[1]
     # workspace
     assert lib.qrb_geqrf_f32(FAKE, FAKE, FAKE, 4, 128, None, 0, None) == 3
@@ -148,7 +148,7 @@ def test_kernel_launch_count(lib):
     assert 64 + 127 * 2 < n32 <= 64 + 127 * 3
     assert lib.qrb_kernel_launches(4096, 2048, 1) == 64 + 127 * 2   # wide batch: no split
     assert lib.qrb_kernel_launches(0, 256, 1) == 0
-    assert lib.qrb_kernel_launches(1, 5000, 1) == 0
+    assert lib.qrb_kernel_launches(1, 8200, 1) == 0
 
 
 def test_kernel_launch_count_bounds(lib):
@@ -204,7 +204,7 @@ def test_host_pipeline_workspace_and_argument_checks(lib):
     assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE, None, 0, 64, None, 0, None) == 0   # empty batch
     assert lib.qrb_qr_f32_host(None, FAKE, FAKE, None, 4, 64, None, 0, None) == 1
     assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE, FAKE, 4, 64, None, 0, None) == 1   # Q aliases A
-    assert lib.qrb_qr_f32_host(FAKE, FAKE + 64, FAKE + 128, None, 4, 5000, None, 0, None) == 2
+    assert lib.qrb_qr_f32_host(FAKE, FAKE + 64, FAKE + 128, None, 4, 8200, None, 0, None) == 2
     need = lib.qrb_host_workspace_size(4, 64, 0)
     assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE + 64, None, 4, 64, FAKE, need - 1, None) == 3
     assert lib.qrb_qr_f32_host(FAKE, FAKE, FAKE + 64, None, 4, 64, FAKE + 16, need, None) == 1

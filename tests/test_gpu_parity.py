@@ -189,6 +189,22 @@ def test_task_yml_specs(spec):
     assert ok, res
 
 
+@pytest.mark.parametrize("n", [4100, 6002, 8192])
+def test_n_beyond_4096(n):
+    """n up to QRB_MAX_N = 8192 (the reference's custom_kernel accepts any n and hands
+    sizes outside its fast paths to torch.geqrf, submission.py:921): panels of more than
+    4096 rows on 16-CTA clusters; n % 4 != 0 takes the SIMT update."""
+    g = torch.Generator(device="cuda").manual_seed(n)
+    A = torch.randn(1, n, n, device="cuda", generator=g)
+    H, tau, Q = qrb().qr(A)
+    ok, res = reference_gate(A, H, tau)
+    assert ok, res
+    a, q, r = A.double(), Q.double(), torch.triu(H).double()
+    recon = (torch.linalg.matrix_norm(q @ r - a) / torch.linalg.matrix_norm(a)).item()
+    assert recon <= TOL_RECON, recon
+    assert (qrb().form_q(H, tau) - Q).abs().max().item() <= 1e-5
+
+
 _WIDE_RAGGED = r"""
 import sys, json
 import numpy as np, torch
