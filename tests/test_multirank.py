@@ -134,3 +134,19 @@ def test_reference_arm_loads_no_repo_library():
     import json
     d = json.loads(r.stdout.strip().splitlines()[-1])
     assert d == {"ok": True, "lib": False, "_entry": False, "ops": False, "same": True}
+
+
+def test_roofline_traffic_from_committed_profiles():
+    """The roofline's DRAM traffic comes from the committed ncu summaries: a per-launch
+    figure, or DRAM bytes per algorithmic byte scaled by the run's bytes per launch; a
+    kernel without a capture reports None rather than another kernel's figure."""
+    import bench
+    t = bench.load_traffic("b32_n2048")
+    assert set(t) >= {"wupdate_kernel", "ygemm_kernel"}
+    r = t["wupdate_kernel"]["dram_per_algorithmic"]
+    assert 0 < r <= 1
+    assert bench.traffic_for(t, "wupdate_kernel", 1e9) == r * 1e9
+    assert bench.traffic_for(t, "panel_kernel", 1e9) is None
+    s = bench.load_traffic("b4096_n64")
+    assert bench.traffic_for(s, "small_qr_kernel", 123.0) == s["small_qr_kernel"]["dram_bytes_per_launch"]
+    assert bench.load_traffic("no_such_config") == {}
